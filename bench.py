@@ -1,0 +1,377 @@
+"""Benchmark of the packed LayerSkip draft/verify step on B200 (driver contract: one JSON line).
+
+Workload (the headline metric's configuration): synthetic LayerSkip-Llama3-8B
+shape, bf16, random init (seed 0) with the residual outputs of layers >= 8 scaled by 0.1,
+B=64 requests per GPU with prompt lengths uniform in [128, 512] (token ids uniform), exit layer 8,
+draft length gamma=4, greedy, 512 new tokens.  The reference's datasets and checkpoints are not
+available; seeded synthetic inputs with these shapes stand in for them.
+
+A "step" is one draft/verify round over the GPU's batch: gamma shallow steps (layers [0, 8) + head)
+and one verify step (the last draft through [0, 8), then 5 tokens per request through [8, 32) +
+head + greedy acceptance).  Multi-GPU runs shard requests (each rank owns its own 64 requests and
+a full weight replica; weak scaling); the only collective is the final gather of the generated
+tokens (NCCL all_gather) inside the timed region.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+``--impl reference`` times the reference algorithm's CPU implementation (the numpy port under
+``oracle/``, fp32 as the reference runs on CPU) on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+B_PER_GPU, EXIT, GAMMA, MAX_NEW = 64, 8, 4, 512
+PROMPT_LEN = (128, 512)
+METRIC = "generated tokens/s/GPU, LayerSkip-8B bf16 B=64 E=8 k=4; verify-step p50 ms"
+WORKLOAD = ("C3: LayerSkip-Llama3-8B-shaped bf16 (32 layers, dim 4096, 32q/8kv heads of 128, SwiGLU 14336, "
+            "vocab 128256, untied), random init seed 0, residual outputs of layers >= 8 scaled by 0.1; "
+            "B=64 requests per GPU, prompts U[128,512], exit layer 8, gamma 4, greedy, 512 new tokens")
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+# ---------------------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.fh,
+                                         stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self) -> dict:
+        if self.proc is None or not self.path:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) >= 9:
+                rows.append(f)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------------- CPU baseline
+def cpu_baseline(tokens_per_round: float, n_samples: int = 1) -> dict:
+    """Reference algorithm on the host cores: the numpy port of common/model.py + packed.py (fp32)
+    at the C3 shapes.  Bounded sample: one shallow layer (64 tokens), one deep layer (64 blocks of
+    5 tokens) at the workload's mean context, and the head on 64 and 320 rows are timed; a round
+    is composed from them (gamma+1 shallow passes of 8 layers, 24 deep layers, gamma+1 heads) and
+    tokens/s uses the tokens per round the GPU engine measured on the same workload."""
+    import numpy as np
+
+    from oracle.model_np import OracleConfig, OracleModel
+    from thesis_b200.config import preset
+
+    try:
+        from threadpoolctl import threadpool_info
+        cores = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
+    except Exception:
+        cores = os.cpu_count() or 1
+    c = preset("llama3-8b")
+    oc = OracleConfig(c.vocab_size, c.dim, 1, c.n_heads, c.n_kv_heads, c.head_dim, c.intermediate_size, c.norm_eps,
+                      c.rope_theta)
+    from thesis_b200.synthetic import layer_shapes
+
+    W = {f"l0.{k}": np.full(s, 0.01, dtype=np.float32) for k, s in layer_shapes(c).items()}
+    W["l0.attn_norm"][:] = 1.0
+    W["l0.ffn_norm"][:] = 1.0
+    # the head GEMM is linear in the vocabulary: time 1/8 of it and scale (keeps host memory small)
+    vshare = 8
+    W["embed"] = np.full((c.vocab_size // vshare, c.dim), 0.01, dtype=np.float32)
+    W["lm_head"] = W["embed"]
+    W["norm"] = np.ones(c.dim, dtype=np.float32)
+    B = B_PER_GPU
+    ctx = (PROMPT_LEN[0] + PROMPT_LEN[1]) // 2 + MAX_NEW // 2          # mean context over a run
+    m = OracleModel(oc, W, False, B, ctx + GAMMA + 64)
+    rng = np.random.default_rng(0)
+    m.kc[:] = rng.standard_normal(m.kc.shape[1:], dtype=np.float32)[None] * 0.1
+    m.vc[:] = m.kc
+    x_sh = rng.standard_normal((B, c.dim), dtype=np.float32)
+    x_dp = rng.standard_normal((B * (GAMMA + 1), c.dim), dtype=np.float32)
+    sh_blocks = [(r, ctx, 1) for r in range(B)]
+    dp_blocks = [(r, ctx - GAMMA, GAMMA + 1) for r in range(B)]
+
+    def layer(x, blocks):
+        T = np.array([b[2] for b in blocks])
+        off = np.concatenate([[0], np.cumsum(T)])
+        pos = np.concatenate([np.arange(p0, p0 + t) for (_, p0, t) in blocks])
+        rows = np.concatenate([np.full(t, r) for (r, _, t) in blocks])
+        t0 = time.perf_counter()
+        m.packed_layer(0, x, blocks, off, pos, rows)
+        return time.perf_counter() - t0
+
+    def head(x):
+        t0 = time.perf_counter()
+        m.head(x)
+        return (time.perf_counter() - t0) * vshare
+
+    samples = []
+    for _ in range(n_samples):
+        t_sh, t_dp, h_sh, h_dp = layer(x_sh, sh_blocks), layer(x_dp, dp_blocks), head(x_sh), head(x_dp)
+        rnd = (GAMMA + 1) * EXIT * t_sh + GAMMA * h_sh + (c.n_layers - EXIT) * t_dp + h_dp
+        samples.append(tokens_per_round / rnd)
+    return {"value": float(statistics.median(samples)), "unit": "tokens/s", "cores": int(cores), "kind": "port",
+            "sample": (f"numpy fp32 port of the reference path at C3 shapes: 1 shallow layer (64 tok), 1 deep layer "
+                       f"(64x5 tok), head on 64 and 320 rows (1/{vshare} of the vocab, x{vshare}) at context {ctx}, composed into a round "
+                       f"(5x8 shallow + 24 deep layers + 5 heads), {tokens_per_round:.1f} tokens/round, "
+                       f"{n_samples} sample(s)")}
+
+
+def run_reference(args) -> None:
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    tpr = args.tokens_per_round
+    for _ in range(args.warmup):
+        cpu_baseline(tpr, 1)
+    t0 = time.perf_counter()
+    cb = cpu_baseline(tpr, max(args.steps, 1))
+    wall = time.perf_counter() - t0
+    line = {"metric": METRIC, "value": cb["value"], "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000 * wall / max(args.steps, 1), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD + " (CPU sample)", "global_batch": B_PER_GPU, "seq_len": MAX_NEW,
+                       "parallelism": "host cores"},
+            "impl": "reference", "cpu_baseline": cb,
+            "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------------- our engine
+def algorithmic(kind: str, n_tok: int, cfg, ctx: float, eb: int = 2) -> tuple[float, float]:
+    """(bytes, flops) of one launch of a runtime kernel kind on n_tok packed tokens."""
+    D, H, Hkv, dim, I = cfg.head_dim, cfg.n_heads, cfg.n_kv_heads, cfg.dim, cfg.intermediate_size
+    shapes = {"gemm_qkv": ((H + 2 * Hkv) * D, dim), "gemm_o": (dim, H * D), "gemm_w13": (2 * I, dim),
+              "gemm_w2": (dim, I), "head": (cfg.vocab_size, dim)}
+    if kind in shapes:
+        n, k = shapes[kind]
+        out = I if kind == "gemm_w13" else n
+        return float(n * k * eb + n_tok * k * eb + n_tok * out * eb), float(2 * n * k * n_tok)
+    if kind == "attn":
+        # KV bytes read per launch: every block reads its context once per KV head
+        return float(ctx * 2 * Hkv * D * eb), float(4 * H * D * ctx * n_tok / max(n_tok, 1))
+    return float(2 * n_tok * dim * eb), 0.0
+
+
+def run_ours(args) -> None:
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from thesis_b200.config import preset
+    from thesis_b200.eesd import B200SpecEngine
+    from thesis_b200.engine import RunConfig
+    from thesis_b200.model import ModelWeights
+    from thesis_b200.synthetic import synthetic_prompts
+    from thesis_b200 import lib
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    cfg = preset("llama3-8b")
+    w = ModelWeights.synthetic(cfg, seed=0, dtype=torch.bfloat16, device=dev, residual_scale_from=EXIT,
+                               residual_scale=0.1)
+    prompts = synthetic_prompts(B_PER_GPU, cfg.vocab_size, seed=1000 + rank, min_len=PROMPT_LEN[0],
+                                max_len=PROMPT_LEN[1])
+    eng = B200SpecEngine(w, B_PER_GPU, PROMPT_LEN[1], MAX_NEW, (), ignore_eos=True, exit_layer=EXIT, gamma=GAMMA)
+    eng.start(prompts)
+    torch.cuda.synchronize()
+    for _ in range(args.warmup):
+        eng.step(measured=False)
+    eng.dm.profile(True)
+    launches0 = eng.dm.launch_count() + lib.direct_launches
+    n_rec0 = len(eng.records)
+    stream = torch.cuda.current_stream()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    committed = 0
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            committed += eng.step(measured=True)
+        if world > 1:          # final output gather (the only collective): tokens generated so far
+            from thesis_b200.shard import gather_outputs
+
+            outs = {rank + world * i: eng.slots[i].output for i in range(B_PER_GPU)}
+            gather_outputs(outs, B_PER_GPU * world, world, device=dev)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    ms = ev0.elapsed_time(ev1)
+    launches = eng.dm.launch_count() + lib.direct_launches - launches0
+    recs = eng.dm.profile_records()
+    eng.dm.profile(False)
+    eng.dm.check()
+    acc_rate = eng.extra_metrics()["spec"]["acceptance_rate"]
+    verify = [r.forward_ms for r in eng.records[n_rec0:] if r.kind == "verify"]
+    draft = [r.forward_ms for r in eng.records[n_rec0:] if r.kind == "draft"]
+    t = torch.tensor([ms, float(committed)], dtype=torch.float64, device=dev)
+    if world > 1:
+        mx = t.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        tot = t.clone()
+        dist.all_reduce(tot, op=dist.ReduceOp.SUM)
+        ms_max, tokens_all = float(mx[0]), float(tot[1])
+    else:
+        ms_max, tokens_all = ms, float(committed)
+    value = tokens_all / (ms_max / 1000.0)
+
+    # ---- dominant kernel group (kind, token count) and its roofline from the live launch timings
+    groups = {}
+    for kind, n_tok, t_ms in recs:
+        g = groups.setdefault((kind, n_tok), [0, 0.0])
+        g[0] += 1
+        g[1] += t_ms
+    (dk, dn), (dcount, dms) = max(groups.items(), key=lambda kv: kv[1][1])
+    pk = peaks()
+    ctx_mean = float(np.mean([s.pos for s in eng.slots]))
+    by, fl = algorithmic(dk, dn, cfg, ctx_mean * B_PER_GPU)
+    avg_s = dms / dcount / 1000.0
+    tensor_bound = fl / max(by, 1.0) > pk["bf16_tflops_sustained"] * 1e12 / (pk["hbm_gbs"] * 1e9)
+    if tensor_bound:
+        achieved, peak, unit = fl / avg_s / 1e12, pk["bf16_tflops_sustained"], "TFLOP/s"
+    else:
+        achieved, peak, unit = by / avg_s / 1e9, pk["hbm_gbs"], "GB/s"
+    total_ms = sum(g[1] for g in groups.values())
+    share = {f"{k}@{n}": round(v[1] / total_ms, 4) for (k, n), v in sorted(groups.items(), key=lambda kv: -kv[1][1])}
+
+    # ---- end to end through the public engine API (host prompts in, token lists out)
+    e2e = None
+    if not args.no_e2e:
+        eng.free()
+        del eng
+        torch.cuda.empty_cache()
+        e2e_eng = B200SpecEngine(w, B_PER_GPU, PROMPT_LEN[1], args.e2e_new, (), ignore_eos=True, exit_layer=EXIT,
+                                 gamma=GAMMA)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        res = e2e_eng.run(prompts, RunConfig(mode="static", keep_outputs=True))
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+        toks = sum(c["generated"] for c in res["completions"])
+        tt = torch.tensor([wall, float(toks)], dtype=torch.float64, device=dev)
+        if world > 1:
+            mx = tt.clone()
+            dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+            tot = tt.clone()
+            dist.all_reduce(tot, op=dist.ReduceOp.SUM)
+            wall, toks = float(mx[0]), float(tot[1])
+        n_steps = max(len(e2e_eng.records), 1)
+        e2e = {"value": toks / wall, "unit": "tokens/s", "h2d_bytes_per_step": int(e2e_eng.h2d_bytes / n_steps),
+               "d2h_bytes_per_step": int(e2e_eng.d2h_bytes / n_steps), "new_tokens_per_request": args.e2e_new,
+               "includes": "prefill of all prompts, every draft/verify step, host bookkeeping"}
+        e2e_eng.free()
+
+    if rank == 0:
+        acc_tokens_per_round = committed / max(args.steps, 1)
+        cb = None if args.no_cpu else cpu_baseline(acc_tokens_per_round, 1)
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "global_batch": B_PER_GPU * world, "seq_len": MAX_NEW,
+                       "parallelism": f"request-sharded x{world}" if world > 1 else "single GPU",
+                       "l2": "inputs larger than L2: each round streams the 16 GB of weights",
+                       "value_is": "aggregate over all GPUs"},
+            "tokens_per_gpu_per_s": value / world,
+            "verify_step_p50_ms": statistics.median(verify) if verify else None,
+            "draft_step_p50_ms": statistics.median(draft) if draft else None,
+            "tokens_per_round_per_gpu": acc_tokens_per_round,
+            "acceptance_rate": acc_rate,
+            "clocks": clk.summary(),
+            "gpu_launches": int(launches),
+            "roofline": {"bound": "tensor" if tensor_bound else "hbm", "achieved": achieved, "peak": peak,
+                         "unit": unit, "frac": achieved / peak, "traffic": None, "kernel": f"{dk}@{dn} tokens",
+                         "launches": dcount, "avg_ms": avg_s * 1000, "peak_source": pk["source"]},
+            "kernel_time_share": share,
+            "e2e": e2e,
+            "cpu_baseline": cb,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-new", type=int, default=MAX_NEW, help="new tokens per request in the end-to-end run")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--tokens-per-round", type=float, default=3.5 * B_PER_GPU,
+                    help="reference arm: tokens committed per round (the GPU engine's measured value)")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,113 @@
+"""Kernel-level numerics on the B200 through the C ABI, against plain PyTorch fp32 references.
+
+bf16 tolerances: every output is rounded to bf16 (relative step 2^-8), so a kernel agrees with
+the fp32 reference within 1e-2 of the output's max magnitude; fp32 kernels within 1e-5.
+"""
+
+import ctypes as C
+
+import numpy as np
+import pytest
+import torch
+
+from thesis_b200 import lib
+
+pytestmark = pytest.mark.gpu
+
+
+def _gemm(x, w, epi=lib.EPI_STORE, residual=None, n_out=None, up_offset=0):
+    n_tok, k = x.shape
+    n_out = n_out or w.shape[0]
+    dt = lib.BF16 if x.dtype == torch.bfloat16 else lib.F32
+    y = torch.empty(n_tok, n_out, dtype=x.dtype, device=x.device)
+    L = lib.load()
+    ws_bytes = L.eesd_gemm_workspace_bytes(n_tok, n_out, k, epi)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
+    lib.call("eesd_gemm", dt, epi, x.data_ptr(), w.data_ptr(), lib.ptr(residual), y.data_ptr(), n_tok, n_out, k,
+             up_offset, ws.data_ptr(), ws_bytes, lib.stream_ptr())
+    bits = C.c_int(0)
+    lib.check(L.eesd_status_read(ws.data_ptr(), C.byref(bits), lib.stream_ptr()), "status")
+    return y
+
+
+def _close(got, ref, tol):
+    got, ref = got.float(), ref.float()
+    err = (got - ref).abs().max().item() / max(ref.abs().max().item(), 1e-30)
+    assert err < tol, err
+
+
+@pytest.mark.parametrize("n_out,k", [(256, 512), (6144, 4096), (4096, 14336), (1000, 1024)])
+@pytest.mark.parametrize("n_tok", [1, 7, 64, 320, 600])
+def test_gemm_bf16_store(cuda_dev, n_out, k, n_tok):
+    g = torch.Generator(device=cuda_dev).manual_seed(n_tok + n_out)
+    x = torch.randn(n_tok, k, device=cuda_dev, generator=g).bfloat16()
+    w = (torch.randn(n_out, k, device=cuda_dev, generator=g) * 0.02).bfloat16()
+    _close(_gemm(x, w), x.float() @ w.float().T, 1e-2)
+
+
+@pytest.mark.parametrize("n_tok", [3, 64, 320])
+def test_gemm_bf16_residual_and_swiglu(cuda_dev, n_tok):
+    g = torch.Generator(device=cuda_dev).manual_seed(7)
+    k, n_out, inter = 1024, 512, 768
+    x = torch.randn(n_tok, k, device=cuda_dev, generator=g).bfloat16()
+    w = (torch.randn(n_out, k, device=cuda_dev, generator=g) * 0.02).bfloat16()
+    r = torch.randn(n_tok, n_out, device=cuda_dev, generator=g).bfloat16()
+    ref = (r.float() + (x.float() @ w.float().T).bfloat16().float()).bfloat16()
+    _close(_gemm(x, w, lib.EPI_RESIDUAL, residual=r), ref, 1e-2)
+    w13 = (torch.randn(2 * inter, k, device=cuda_dev, generator=g) * 0.05).bfloat16()
+    gu = (x.float() @ w13.float().T).bfloat16().float()
+    gg, uu = gu[:, :inter], gu[:, inter:]
+    ref = (torch.nn.functional.silu(gg).bfloat16().float() * uu).bfloat16()
+    _close(_gemm(x, w13, lib.EPI_SWIGLU, n_out=inter, up_offset=inter), ref, 1e-2)
+
+
+@pytest.mark.parametrize("mma_n", [0, 64])
+def test_gemm_bf16_is_batch_invariant(cuda_dev, mma_n):
+    """A token row's result is bit-identical whatever the number of tokens in the launch."""
+    g = torch.Generator(device=cuda_dev).manual_seed(3)
+    k, n_out = 4096, 6144
+    x = torch.randn(640, k, device=cuda_dev, generator=g).bfloat16()
+    w = (torch.randn(n_out, k, device=cuda_dev, generator=g) * 0.02).bfloat16()
+    lib.call("eesd_set_option", lib.OPT_MMA_N, mma_n)
+    try:
+        full = _gemm(x, w)
+        for n in (1, 4, 16, 64, 100, 320, 333):
+            assert torch.equal(_gemm(x[:n].contiguous(), w), full[:n]), n
+    finally:
+        lib.call("eesd_set_option", lib.OPT_MMA_N, 0)
+
+
+@pytest.mark.parametrize("n_tok", [1, 70, 300])
+def test_gemm_f32(cuda_dev, n_tok):
+    g = torch.Generator(device=cuda_dev).manual_seed(1)
+    x = torch.randn(n_tok, 512, device=cuda_dev, generator=g)
+    w = torch.randn(384, 512, device=cuda_dev, generator=g) * 0.02
+    r = torch.randn(n_tok, 384, device=cuda_dev, generator=g)
+    _close(_gemm(x, w), x @ w.T, 1e-5)
+    _close(_gemm(x, w, lib.EPI_RESIDUAL, residual=r), r + x @ w.T, 1e-5)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_rmsnorm(cuda_dev, dtype):
+    g = torch.Generator(device=cuda_dev).manual_seed(2)
+    x = torch.randn(37, 4096, device=cuda_dev, generator=g).to(dtype)
+    w = (1 + 0.1 * torch.randn(4096, device=cuda_dev, generator=g)).to(dtype)
+    rows = torch.tensor([5, 0, 36, 5], dtype=torch.int32, device=cuda_dev)
+    y = torch.empty(4, 4096, dtype=dtype, device=cuda_dev)
+    lib.call("eesd_rmsnorm", lib.BF16 if dtype == torch.bfloat16 else lib.F32, x.data_ptr(), rows.data_ptr(),
+             w.data_ptr(), y.data_ptr(), 4, 4096, 1e-5, lib.stream_ptr())
+    xf = x[rows.long()].float()
+    ref = w * (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-5)).to(dtype)
+    _close(y, ref, 1e-2 if dtype == torch.bfloat16 else 1e-5)
+
+
+def test_greedy_accept(cuda_dev):
+    cols = 5
+    seq = torch.tensor([[9, 1, 2, 3, 4], [9, 5, 6, 7, 8], [9, 1, 1, 1, 1]], dtype=torch.int32, device=cuda_dev)
+    y = torch.tensor([1, 2, 0, 3, 4,    5, 6, 7, 8, 11,    2, 1, 1, 1, 1], dtype=torch.int32, device=cuda_dev)
+    vinfo = torch.tensor([[0, 5, 0], [5, 5, 1], [10, 5, 2]], dtype=torch.int32, device=cuda_dev)
+    acc = torch.empty(3, dtype=torch.int32, device=cuda_dev)
+    lib.call("eesd_greedy_accept", y.data_ptr(), vinfo.data_ptr(), 3, seq.data_ptr(), cols, acc.data_ptr(),
+             lib.stream_ptr())
+    assert acc.tolist() == [2, 4, 0]
+    assert seq[:, 0].tolist() == [0, 11, 2]

@@ -1,0 +1,409 @@
+// tcgen05 / TMEM bf16 GEMM for the packed token axis:  Y[t, o] = epi( sum_k X[t, k] * W[o, k] ).
+//
+// Replaces the F.linear calls of solutions/packed.py:175-185 (QKV, O + residual, W13 + SwiGLU,
+// W2 + residual) and the LM head of common/model.py:328-330 (+ argmax).
+//
+// Mapping: the weight is the MMA "A" operand (M = 128 output features per CTA), the packed
+// tokens are "B" (N = token tile, <= 256), both K-major in shared memory with 128-byte
+// swizzle, staged by TMA; the fp32 accumulator lives in TMEM (128 lanes x N columns).
+//   warp 0      TMA producer (one elected lane), STAGES-deep ring of (W tile, X tile)
+//   warp 1      TMEM allocator + MMA issuer (one lane), tcgen05.commit frees a stage
+//   warps 2..5  epilogue: tcgen05.ld of their 32-lane quadrant, fused epilogue, stores
+// SwiGLU keeps two accumulators (gate rows o and up rows o + I) in the same TMEM lanes, so
+// silu(g) * u is formed per thread with no data exchange.
+//
+// Batch invariance (needed for bit-exact speculative == autoregressive output): the K range
+// of every split and the split count depend only on the weight shape, partial sums are
+// reduced in split order by the last CTA of a tile, and every token column is an
+// independent dot product.  No atomics touch values except the order-free argmax max().
+#include <algorithm>
+#include <cstdio>
+#include <mutex>
+
+#include "common.cuh"
+#include "gemm_tc.h"
+
+namespace eesd {
+
+namespace {
+
+constexpr int kBM = 128;   // output features per CTA (MMA M)
+constexpr int kBK = 64;    // K per stage: 64 bf16 = one 128-byte swizzle row
+constexpr int kThreads = 192;
+constexpr uint32_t kATileBytes = kBM * kBK * 2;
+constexpr size_t kSmemBudget = 200 * 1024;
+
+struct alignas(8) TcParams {
+  int n_tok, n_out, K;
+  int bn;           // token tile (multiple of mma_n)
+  int mma_n;        // N of one tcgen05.mma (multiple of 16, <= 256)
+  int kb_total;     // ceil(K / 64)
+  int kb_per;       // k-blocks per split
+  int splits;
+  int stages;
+  int up_offset;    // SwiGLU: row of the first 'up' weight
+  int tmem_cols;
+  const bf16* residual;
+  int ld_res;
+  bf16* y;
+  int ld_y;
+  float* partial;   // [splits][n_tok][ld_p]
+  int ld_p;
+  int* counters;    // [tok_tiles * out_tiles], zero between launches
+  unsigned long long* keys;  // argmax keys [n_tok]
+  int* status;
+};
+
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+template <int EPI>
+__device__ __forceinline__ void epilogue_store(const TcParams& p, int t, int row, float g, float u) {
+  const size_t o = (size_t)t * p.ld_y + row;
+  if (EPI == EESD_EPI_STORE) {
+    p.y[o] = __float2bfloat16_rn(g);
+  } else if (EPI == EESD_EPI_RESIDUAL) {
+    // x + F.linear(...): the product is rounded to bf16 first, then the bf16 add rounds again
+    const float r = __bfloat162float(p.residual[(size_t)t * p.ld_res + row]);
+    p.y[o] = __float2bfloat16_rn(r + rnd<bf16>(g));
+  } else if (EPI == EESD_EPI_SWIGLU) {
+    // F.silu(g) * u in bf16: g, u rounded (F.linear output), silu rounded, product rounded
+    const float gb = rnd<bf16>(g), ub = rnd<bf16>(u);
+    const float s = rnd<bf16>(gb / (1.0f + expf(-gb)));
+    p.y[o] = __float2bfloat16_rn(s * ub);
+  }
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x, TcParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int kNA = (EPI == EESD_EPI_SWIGLU) ? 2 : 1;
+  const uint32_t b_bytes = (uint32_t)p.bn * kBK * 2;
+  const uint32_t stage_bytes = kNA * kATileBytes + b_bytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)p.stages * stage_bytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + p.stages;
+  uint64_t* accb = bars + 2 * p.stages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accb + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* last_flag = reinterpret_cast<int*>(tmem_slot + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tok_tile = blockIdx.x, out_tile = blockIdx.y, split = blockIdx.z;
+  const int n0 = tok_tile * p.bn, m0 = out_tile * kBM;
+  const int kb_begin = split * p.kb_per;
+  const int nkb = min(p.kb_total, kb_begin + p.kb_per) - kb_begin;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < p.stages; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+    }
+    mbar_init(smem_u32(accb), 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&map_w);
+    tma_prefetch_desc(&map_x);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), (uint32_t)p.tmem_cols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % p.stages, r = i / p.stages;
+        if (r > 0 && !mbar_wait(smem_u32(&empty[s]), (r - 1) & 1, abort_flag)) {
+          set_status(p.status, kStatusTimeoutProducer);
+          *abort_flag = 1;
+          break;
+        }
+        const uint32_t fb = smem_u32(&full[s]);
+        mbar_arrive_expect_tx(fb, stage_bytes);
+        const uint32_t st = smem_u32(smem + (size_t)s * stage_bytes);
+        const int kx = (kb_begin + i) * kBK;
+        tma_load_2d(st, &map_w, kx, m0, fb);
+        if (kNA == 2) tma_load_2d(st + kATileBytes, &map_w, kx, p.up_offset + m0, fb);
+        tma_load_2d(st + kNA * kATileBytes, &map_x, kx, n0, fb);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_bf16_f32(kBM, p.mma_n);
+      bool ok = true;
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % p.stages, r = i / p.stages;
+        if (!mbar_wait(smem_u32(&full[s]), r & 1, abort_flag)) {
+          set_status(p.status, kStatusTimeoutMma);
+          *abort_flag = 1;
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a0 = smem_u32(smem + (size_t)s * stage_bytes);
+        const uint32_t b0 = a0 + kNA * kATileBytes;
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk) {
+          const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+          for (int nb = 0; nb < p.bn; nb += p.mma_n) {
+            const uint64_t bd = sw128_kmajor_desc(b0 + (uint32_t)nb * 128u + kk * 32u);
+            tc_mma_f16(tmem_base + nb, sw128_kmajor_desc(a0 + kk * 32u), bd, idesc, acc);
+            if (kNA == 2) tc_mma_f16(tmem_base + p.bn + nb, sw128_kmajor_desc(a0 + kATileBytes + kk * 32u), bd, idesc, acc);
+          }
+        }
+        tc_commit(smem_u32(&empty[s]));
+      }
+      if (ok) tc_commit(smem_u32(accb));
+    }
+  } else {
+    // ---------------- epilogue: warps 2..5 own TMEM lane quadrants (warp % 4)
+    const int q = warp & 3;
+    const int row = m0 + q * 32 + lane;
+    const bool row_ok = row < p.n_out;
+    const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16);
+    const bool ok = mbar_wait(smem_u32(accb), 0, abort_flag);
+    if (!ok) {
+      set_status(p.status, kStatusTimeoutEpilogue);
+      *abort_flag = 1;
+    }
+    tc_fence_after();
+    if (ok) {
+      if (p.splits == 1) {
+        if (EPI == EESD_EPI_STORE || EPI == EESD_EPI_RESIDUAL || EPI == EESD_EPI_SWIGLU) {
+          for (int c = 0; c < p.bn; c += 16) {
+            float v[16], u[16];
+            tmem_ld16(lane_base + c, v);
+            if (EPI == EESD_EPI_SWIGLU) tmem_ld16(lane_base + p.bn + c, u);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int t = n0 + c + j;
+              if (t < p.n_tok && row_ok) epilogue_store<EPI>(p, t, row, v[j], EPI == EESD_EPI_SWIGLU ? u[j] : 0.f);
+            }
+          }
+        } else {  // ARGMAX: logits rounded to bf16, max over this CTA's 128 rows, then atomicMax
+          unsigned long long* red = reinterpret_cast<unsigned long long*>(smem);  // stage memory is free now
+          for (int c = 0; c < p.bn; c += 16) {
+            float v[16];
+            tmem_ld16(lane_base + c, v);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              unsigned long long key = row_ok ? argmax_key(rnd<bf16>(v[j]), (uint32_t)row) : 0ull;
+#pragma unroll
+              for (int off = 16; off > 0; off >>= 1) {
+                const unsigned long long o = __shfl_xor_sync(0xffffffffu, key, off);
+                key = o > key ? o : key;
+              }
+              if (lane == 0) red[(c + j) * 4 + q] = key;
+            }
+          }
+          epi_bar();
+          for (int c = threadIdx.x - 64; c < p.bn; c += 128) {
+            const int t = n0 + c;
+            if (t < p.n_tok) {
+              unsigned long long k = red[c * 4];
+              for (int w = 1; w < 4; ++w) k = red[c * 4 + w] > k ? red[c * 4 + w] : k;
+              atomicMax(&p.keys[t], k);
+            }
+          }
+        }
+      } else {
+        // ---------------- split-K: publish fp32 partials, the last CTA of the tile reduces in split order
+        constexpr int kParts = (EPI == EESD_EPI_SWIGLU) ? 2 : 1;
+        float* mine = p.partial + (size_t)split * p.n_tok * p.ld_p;
+        for (int c = 0; c < p.bn; c += 16) {
+          float v[16], u[16];
+          tmem_ld16(lane_base + c, v);
+          if (kParts == 2) tmem_ld16(lane_base + p.bn + c, u);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int t = n0 + c + j;
+            if (t < p.n_tok && row_ok) {
+              mine[(size_t)t * p.ld_p + row] = v[j];
+              if (kParts == 2) mine[(size_t)t * p.ld_p + p.n_out + row] = u[j];
+            }
+          }
+        }
+        __threadfence();
+        epi_bar();
+        if (threadIdx.x == 64) {
+          const int tile = out_tile * gridDim.x + tok_tile;
+          const int old = atomicAdd(&p.counters[tile], 1);
+          *last_flag = (old == p.splits - 1);
+          if (old == p.splits - 1) p.counters[tile] = 0;   // ready for the next launch
+        }
+        epi_bar();
+        if (*last_flag) {
+          __threadfence();
+          const int t_end = min(p.n_tok, n0 + p.bn);
+          if (row_ok) {
+            for (int t = n0; t < t_end; ++t) {
+              float g = 0.f, u = 0.f;
+              for (int s = 0; s < p.splits; ++s) {
+                const float* ps = p.partial + ((size_t)s * p.n_tok + t) * p.ld_p;
+                g += __ldcg(ps + row);
+                if (kParts == 2) u += __ldcg(ps + p.n_out + row);
+              }
+              epilogue_store<EPI>(p, t, row, g, u);
+            }
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, (uint32_t)p.tmem_cols);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+PFN_encodeTiled_t g_encode = nullptr;
+std::once_flag g_encode_once;
+int g_mma_n_option = 0;   // 0: one MMA spans the whole token tile
+
+int next_pow2(int v) {
+  int p = 32;
+  while (p < v) p <<= 1;
+  return p;
+}
+
+template <int EPI>
+int ensure_smem_attr(size_t bytes) {
+  static size_t set = 0;
+  if (bytes > set) {
+    if (cudaFuncSetAttribute(tc_gemm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) !=
+        cudaSuccess)
+      return EESD_ERR_CUDA;
+    set = bytes;
+  }
+  return EESD_OK;
+}
+
+}  // namespace
+
+PFN_encodeTiled_t tensor_map_encoder() {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_encodeTiled_t>(fn);
+  });
+  return g_encode;
+}
+
+int encode_kmajor_map(CUtensorMap* map, const void* base, int rows, int k, int box_rows) {
+  PFN_encodeTiled_t enc = tensor_map_encoder();
+  if (!enc) return EESD_ERR_CUDA;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (k % 8) || box_rows < 1 || box_rows > 256) return EESD_ERR_ARG;
+  cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)k * 2};
+  cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? EESD_OK : EESD_ERR_CUDA;
+}
+
+void tc_set_mma_n(int n) { g_mma_n_option = n; }
+
+TcPlan tc_plan(int n_tok, int n_out, int k, int epi) {
+  TcPlan pl{};
+  const int mma_fixed = g_mma_n_option;
+  pl.tok_tiles = (n_tok + 255) / 256;
+  const int per = (n_tok + pl.tok_tiles - 1) / pl.tok_tiles;
+  if (mma_fixed > 0) {
+    pl.mma_n = mma_fixed;
+    pl.bn = (per + mma_fixed - 1) / mma_fixed * mma_fixed;
+    if (pl.bn > 256) pl.bn = 256 / mma_fixed * mma_fixed;
+    pl.tok_tiles = (n_tok + pl.bn - 1) / pl.bn;
+  } else {
+    pl.bn = std::max(16, (per + 15) / 16 * 16);
+    pl.mma_n = pl.bn;
+  }
+  pl.out_tiles = (n_out + kBM - 1) / kBM;
+  pl.kb_total = (k + kBK - 1) / kBK;
+  // split count from the weight shape only (never from n_tok): about one wave of 148 SMs at
+  // one token tile, with at least 8 k-blocks (512 of K) per split
+  int s = 1;
+  if (epi != EESD_EPI_ARGMAX_INTERNAL) s = std::max(1, std::min(148 / std::max(pl.out_tiles, 1), pl.kb_total / 8));
+  pl.kb_per = (pl.kb_total + s - 1) / s;
+  pl.splits = (pl.kb_total + pl.kb_per - 1) / pl.kb_per;
+  const int na = epi == EESD_EPI_SWIGLU ? 2 : 1;
+  const size_t stage = (size_t)na * kATileBytes + (size_t)pl.bn * kBK * 2;
+  pl.stages = (int)std::min<size_t>(8, kSmemBudget / stage);
+  pl.smem = (size_t)pl.stages * stage + 1024 + 256;
+  pl.tmem_cols = next_pow2(na * pl.bn);
+  pl.ld_p = epi == EESD_EPI_SWIGLU ? 2 * n_out : n_out;
+  pl.partial_floats = pl.splits > 1 ? (size_t)pl.splits * n_tok * pl.ld_p : 0;
+  pl.counters = pl.splits > 1 ? (size_t)pl.tok_tiles * pl.out_tiles : 0;
+  return pl;
+}
+
+int tc_gemm_launch(int epi, const CUtensorMap& map_w, const void* x, int n_tok, int n_out, int k, int up_offset,
+                   const void* residual, int ld_res, void* y, int ld_y, float* partial, int* counters,
+                   unsigned long long* keys, int* status, cudaStream_t stream) {
+  if (n_tok <= 0 || n_out <= 0 || k <= 0) return EESD_ERR_ARG;
+  const TcPlan pl = tc_plan(n_tok, n_out, k, epi);
+  if (pl.splits > 1 && (!partial || !counters)) return EESD_ERR_ARG;
+  if (pl.stages < 2) return EESD_ERR_ARG;
+  CUtensorMap map_x;
+  int rc = encode_kmajor_map(&map_x, x, n_tok, k, pl.bn);
+  if (rc) return rc;
+  TcParams p{};
+  p.n_tok = n_tok;
+  p.n_out = n_out;
+  p.K = k;
+  p.bn = pl.bn;
+  p.mma_n = pl.mma_n;
+  p.kb_total = pl.kb_total;
+  p.kb_per = pl.kb_per;
+  p.splits = pl.splits;
+  p.stages = pl.stages;
+  p.up_offset = up_offset;
+  p.tmem_cols = pl.tmem_cols;
+  p.residual = static_cast<const bf16*>(residual);
+  p.ld_res = ld_res;
+  p.y = static_cast<bf16*>(y);
+  p.ld_y = ld_y;
+  p.partial = partial;
+  p.ld_p = pl.ld_p;
+  p.counters = counters;
+  p.keys = keys;
+  p.status = status;
+  dim3 grid(pl.tok_tiles, pl.out_tiles, pl.splits);
+  switch (epi) {
+    case EESD_EPI_STORE:
+      if ((rc = ensure_smem_attr<EESD_EPI_STORE>(pl.smem))) return rc;
+      tc_gemm_kernel<EESD_EPI_STORE><<<grid, kThreads, pl.smem, stream>>>(map_w, map_x, p);
+      break;
+    case EESD_EPI_RESIDUAL:
+      if ((rc = ensure_smem_attr<EESD_EPI_RESIDUAL>(pl.smem))) return rc;
+      tc_gemm_kernel<EESD_EPI_RESIDUAL><<<grid, kThreads, pl.smem, stream>>>(map_w, map_x, p);
+      break;
+    case EESD_EPI_SWIGLU:
+      if ((rc = ensure_smem_attr<EESD_EPI_SWIGLU>(pl.smem))) return rc;
+      tc_gemm_kernel<EESD_EPI_SWIGLU><<<grid, kThreads, pl.smem, stream>>>(map_w, map_x, p);
+      break;
+    case EESD_EPI_ARGMAX_INTERNAL:
+      if ((rc = ensure_smem_attr<EESD_EPI_ARGMAX_INTERNAL>(pl.smem))) return rc;
+      tc_gemm_kernel<EESD_EPI_ARGMAX_INTERNAL><<<grid, kThreads, pl.smem, stream>>>(map_w, map_x, p);
+      break;
+    default:
+      return EESD_ERR_ARG;
+  }
+  return cudaPeekAtLastError() == cudaSuccess ? EESD_OK : EESD_ERR_CUDA;
+}
+
+}  // namespace eesd

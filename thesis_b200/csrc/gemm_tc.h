@@ -1,0 +1,30 @@
+// Internal interface of the tcgen05 GEMM (not part of the C ABI).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+
+#define EESD_EPI_ARGMAX_INTERNAL 3   // head: logits rounded to bf16 -> per-token argmax keys
+
+namespace eesd {
+
+typedef CUresult (*PFN_encodeTiled_t)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                      const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                      CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+struct TcPlan {
+  int tok_tiles, out_tiles, bn, mma_n, kb_total, kb_per, splits, stages, tmem_cols, ld_p;
+  size_t smem, partial_floats, counters;
+};
+
+PFN_encodeTiled_t tensor_map_encoder();
+// 2-D K-major bf16 map [rows, k] with a (64 x box_rows) box and 128-byte swizzle
+int encode_kmajor_map(CUtensorMap* map, const void* base, int rows, int k, int box_rows);
+TcPlan tc_plan(int n_tok, int n_out, int k, int epi);
+void tc_set_mma_n(int n);
+int tc_gemm_launch(int epi, const CUtensorMap& map_w, const void* x, int n_tok, int n_out, int k, int up_offset,
+                   const void* residual, int ld_res, void* y, int ld_y, float* partial, int* counters,
+                   unsigned long long* keys, int* status, cudaStream_t stream);
+
+}  // namespace eesd

@@ -1,0 +1,679 @@
+// Non-GEMM kernels of the packed draft/verify step: RMSNorm, RoPE + in-place KV append,
+// varlen GQA attention over the static per-row KV cache, embedding / row gathers, greedy
+// acceptance, argmax, and the fp32 (CUDA-core) GEMM of the parity path.
+#include <math.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace eesd {
+
+namespace {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// ---------------------------------------------------------------- RMSNorm (common/model.py:153-156)
+// y = w * round(x * rsqrt(mean(x^2) + eps)); the sum of squares has a fixed per-row order
+// (thread-strided partial sums, then a fixed tree), so a row's result never depends on
+// which other rows share the launch.
+template <typename T>
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const T* __restrict__ x, const int32_t* __restrict__ rows,
+                                                      const T* __restrict__ w, T* __restrict__ y, int dim, float eps) {
+  __shared__ float red[8];
+  const int i = blockIdx.x;
+  const int src = rows ? rows[i] : i;
+  const T* xr = x + (size_t)src * dim;
+  float ss = 0.f;
+  for (int j = threadIdx.x; j < dim; j += 256) {
+    const float v = to_f(xr[j]);
+    ss = fmaf(v, v, ss);
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int k = 0; k < 8; ++k) t += red[k];
+    red[0] = rsqrtf(t / (float)dim + eps);
+  }
+  __syncthreads();
+  const float r = red[0];
+  T* yr = y + (size_t)i * dim;
+  for (int j = threadIdx.x; j < dim; j += 256) yr[j] = from_f<T>(to_f(w[j]) * rnd<T>(to_f(xr[j]) * r));
+}
+
+// ---------------------------------------------------------------- RoPE + KV append
+// common/model.py:143-150 and solutions/packed.py:176-181: q, k rotated in the rotate-half
+// layout with cos/sin cast to the model dtype; q written back in place, k and v written into
+// the cache at (row, kv head, position).  Rollback needs no kernel: stale positions beyond a
+// row's committed length are never read.
+template <typename T>
+__global__ void __launch_bounds__(128) rope_kv_kernel(T* __restrict__ qkv, const int32_t* __restrict__ tok_pos,
+                                                      const int32_t* __restrict__ tok_row, int n_heads,
+                                                      int n_kv_heads, int D, const float* __restrict__ cosb,
+                                                      const float* __restrict__ sinb, T* __restrict__ kc,
+                                                      T* __restrict__ vc, int max_batch, int max_seq, int* status) {
+  const int t = blockIdx.x;
+  const int pos = tok_pos[t], row = tok_row[t];
+  if (pos < 0 || pos >= max_seq || row < 0 || row >= max_batch) {
+    if (threadIdx.x == 0) set_status(status, kStatusBadIndex);
+    return;
+  }
+  const int half = D / 2;
+  const int ldq = (n_heads + 2 * n_kv_heads) * D;
+  T* base = qkv + (size_t)t * ldq;
+  const float* cr = cosb + (size_t)pos * D;
+  const float* sr = sinb + (size_t)pos * D;
+  const int n_rot = (n_heads + n_kv_heads) * half;
+  for (int idx = threadIdx.x; idx < n_rot; idx += blockDim.x) {
+    const int h = idx / half, d = idx - h * half;
+    T* xh = base + h * D;     // heads 0..Hq-1 are q, Hq.. are k (contiguous in the fused row)
+    const float x1 = to_f(xh[d]), x2 = to_f(xh[d + half]);
+    const float c1 = rnd<T>(cr[d]), c2 = rnd<T>(cr[d + half]);
+    const float s1 = rnd<T>(sr[d]), s2 = rnd<T>(sr[d + half]);
+    const T o1 = from_f<T>(rnd<T>(x1 * c1) + rnd<T>(-x2 * s1));
+    const T o2 = from_f<T>(rnd<T>(x2 * c2) + rnd<T>(x1 * s2));
+    if (h < n_heads) {
+      xh[d] = o1;
+      xh[d + half] = o2;
+    } else {
+      T* dst = kc + (((size_t)row * n_kv_heads + (h - n_heads)) * max_seq + pos) * D;
+      dst[d] = o1;
+      dst[d + half] = o2;
+    }
+  }
+  const T* v = base + (n_heads + n_kv_heads) * D;
+  for (int idx = threadIdx.x; idx < n_kv_heads * D; idx += blockDim.x) {
+    const int h = idx / D, d = idx - h * D;
+    vc[(((size_t)row * n_kv_heads + h) * max_seq + pos) * D + d] = v[idx];
+  }
+}
+
+// ---------------------------------------------------------------- attention
+// One CTA per (work item, KV head).  A work item is up to `item_tokens` consecutive tokens of
+// one block; its query rows are (token, q head of this KV group), GQA folded into rows as in
+// solutions/packed.py:158.  Key tiles start at absolute position 0 and are visited in order,
+// so a query's result does not depend on the other queries of the launch (a fully masked
+// tile leaves the running max, sum and output unchanged).
+
+// fp32 (parity path): scalar online softmax, one warp per query row.
+template <int D>
+__global__ void __launch_bounds__(128) attn_f32_kernel(AttnGeom g, int item_tokens, const float* __restrict__ q,
+                                                       const float* __restrict__ kc, const float* __restrict__ vc,
+                                                       float* __restrict__ out, const int32_t* __restrict__ blk,
+                                                       const int32_t* __restrict__ items) {
+  constexpr int KT = 32, DP = D + 1, ND = D / 32, MAXR = 16;
+  extern __shared__ float sm[];
+  float* Qs = sm;                   // [64][D]
+  float* Ks = Qs + 64 * D;          // [KT][DP]
+  float* Vs = Ks + KT * DP;         // [KT][D]
+  const int item = blockIdx.x, kvh = blockIdx.y;
+  const int b = items[2 * item], t0 = items[2 * item + 1];
+  const int start = blk[4 * b], T = blk[4 * b + 1], row = blk[4 * b + 2], pos0 = blk[4 * b + 3];
+  const int G = g.n_heads / g.n_kv_heads;
+  const int nt = min(item_tokens, T - t0);
+  const int nrows = nt * G;
+  const int kv_len = pos0 + t0 + nt;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int idx = threadIdx.x; idx < nrows * D; idx += blockDim.x) {
+    const int r = idx / D, d = idx - r * D;
+    Qs[idx] = q[(size_t)(start + t0 + r / G) * g.ld_q + (kvh * G + r % G) * D + d];
+  }
+  const float* Kb = kc + ((size_t)row * g.n_kv_heads + kvh) * g.max_seq * D;
+  const float* Vb = vc + ((size_t)row * g.n_kv_heads + kvh) * g.max_seq * D;
+  float m[MAXR], l[MAXR], acc[MAXR][ND];
+#pragma unroll
+  for (int i = 0; i < MAXR; ++i) {
+    m[i] = -INFINITY;
+    l[i] = 0.f;
+#pragma unroll
+    for (int e = 0; e < ND; ++e) acc[i][e] = 0.f;
+  }
+  for (int k0 = 0; k0 < kv_len; k0 += KT) {
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < KT * D; idx += blockDim.x) {
+      const int j = idx / D, d = idx - j * D;
+      const bool in = k0 + j < kv_len;
+      Ks[j * DP + d] = in ? Kb[(size_t)(k0 + j) * D + d] : 0.f;
+      Vs[j * D + d] = in ? Vb[(size_t)(k0 + j) * D + d] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < MAXR; ++i) {
+      const int r = warp + 4 * i;
+      if (r < nrows) {
+        const int qpos = pos0 + t0 + r / G;
+        const int key = k0 + lane;
+        const bool valid = key <= qpos;
+        float s = -INFINITY;
+        if (valid) {
+          float dot = 0.f;
+          for (int d = 0; d < D; ++d) dot = fmaf(Qs[r * D + d], Ks[lane * DP + d], dot);
+          s = dot * g.scale;
+        }
+        const float mt = warp_max(s);
+        const float mn = fmaxf(m[i], mt);
+        const float corr = expf(m[i] - mn);
+        const float p = valid ? expf(s - mn) : 0.f;
+        l[i] = l[i] * corr + warp_sum(p);
+#pragma unroll
+        for (int e = 0; e < ND; ++e) {
+          float a = acc[i][e] * corr;
+          for (int j = 0; j < KT; ++j) a = fmaf(__shfl_sync(0xffffffffu, p, j), Vs[j * D + e * 32 + lane], a);
+          acc[i][e] = a;
+        }
+        m[i] = mn;
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < MAXR; ++i) {
+    const int r = warp + 4 * i;
+    if (r < nrows) {
+      float* o = out + (size_t)(start + t0 + r / G) * g.n_heads * D + (kvh * G + r % G) * D;
+#pragma unroll
+      for (int e = 0; e < ND; ++e) o[e * 32 + lane] = acc[i][e] / l[i];
+    }
+  }
+}
+
+// bf16: tensor-core (mma.sync m16n8k16) flash-decoding over 64-key tiles staged in shared
+// memory by cp.async (double buffered); each warp owns 16 query rows, softmax in fp32 registers.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool fill) {
+  const int sz = fill ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(sz) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N> __device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void mma_bf16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+template <int D>
+__global__ void __launch_bounds__(128) attn_bf16_kernel(AttnGeom g, int item_tokens, const bf16* __restrict__ q,
+                                                        const bf16* __restrict__ kc, const bf16* __restrict__ vc,
+                                                        bf16* __restrict__ out, const int32_t* __restrict__ blk,
+                                                        const int32_t* __restrict__ items) {
+  constexpr int KT = 64;              // keys per tile
+  constexpr int LD = D + 8;           // padded row (elements): conflict-free ldmatrix
+  constexpr int NK = KT / 8;          // score n-tiles per key tile
+  constexpr int ND = D / 8;           // output n-tiles
+  extern __shared__ __align__(16) uint8_t smem8[];
+  bf16* Qs = reinterpret_cast<bf16*>(smem8);           // [64][LD]
+  bf16* Ks = Qs + 64 * LD;                              // [2][KT][LD]
+  bf16* Vs = Ks + 2 * KT * LD;                          // [2][KT][LD]
+
+  const int item = blockIdx.x, kvh = blockIdx.y;
+  const int b = items[2 * item], t0 = items[2 * item + 1];
+  const int start = blk[4 * b], T = blk[4 * b + 1], row = blk[4 * b + 2], pos0 = blk[4 * b + 3];
+  const int G = g.n_heads / g.n_kv_heads;
+  const int nt = min(item_tokens, T - t0);
+  const int nrows = nt * G;
+  const int kv_len = pos0 + t0 + nt;
+  const int n_tiles = (kv_len + KT - 1) / KT;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bf16* Kb = kc + ((size_t)row * g.n_kv_heads + kvh) * g.max_seq * D;
+  const bf16* Vb = vc + ((size_t)row * g.n_kv_heads + kvh) * g.max_seq * D;
+
+  // Q rows (row r = token r / G, head kvh*G + r % G); rows >= nrows are zero
+  constexpr int CPR = D / 8;   // 16-byte chunks per row
+  for (int c = threadIdx.x; c < 64 * CPR; c += 128) {
+    const int r = c / CPR, cc = c - r * CPR;
+    const bool in = r < nrows;
+    const bf16* src = in ? q + (size_t)(start + t0 + r / G) * g.ld_q + (kvh * G + r % G) * D + cc * 8 : q;
+    cp_async16(smem_u32(Qs + r * LD + cc * 8), src, in);
+  }
+  auto load_tile = [&](int tile, int buf) {
+    const int k0 = tile * KT;
+    for (int c = threadIdx.x; c < KT * CPR; c += 128) {
+      const int j = c / CPR, cc = c - j * CPR;
+      const bool in = k0 + j < kv_len;
+      const size_t off = in ? (size_t)(k0 + j) * D + cc * 8 : 0;
+      cp_async16(smem_u32(Ks + (buf * KT + j) * LD + cc * 8), Kb + off, in);
+      cp_async16(smem_u32(Vs + (buf * KT + j) * LD + cc * 8), Vb + off, in);
+    }
+  };
+  load_tile(0, 0);
+  cp_async_commit();
+
+  const int gq = lane >> 2, tq = lane & 3;
+  const int r0 = warp * 16 + gq, r1 = r0 + 8;
+  const int qpos0 = r0 < nrows ? pos0 + t0 + r0 / G : -1;
+  const int qpos1 = r1 < nrows ? pos0 + t0 + r1 / G : -1;
+  const bool warp_active = warp * 16 < nrows;
+  float o[ND][4];
+#pragma unroll
+  for (int n = 0; n < ND; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  uint32_t qa[D / 16][4];
+
+  for (int tile = 0; tile < n_tiles; ++tile) {
+    const int buf = tile & 1;
+    if (tile + 1 < n_tiles) load_tile(tile + 1, buf ^ 1);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    if (tile == 0 && warp_active) {
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const bf16* p = Qs + (warp * 16 + (lane & 15)) * LD + kk * 16 + (lane >> 4) * 8;
+        ldsm_x4(smem_u32(p), qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3]);
+      }
+    }
+    if (warp_active) {
+      const bf16* Kt = Ks + buf * KT * LD;
+      const bf16* Vt = Vs + buf * KT * LD;
+      float s[NK][4];
+#pragma unroll
+      for (int n = 0; n < NK; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) {
+#pragma unroll
+        for (int n2 = 0; n2 < NK; n2 += 2) {
+          // keys n2*8 .. n2*8+15, dims kk*16 .. +15
+          const int key = n2 * 8 + (lane & 7) + ((lane >> 4) << 3);
+          const int dim = kk * 16 + ((lane >> 3) & 1) * 8;
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4(smem_u32(Kt + key * LD + dim), b0, b1, b2, b3);
+          mma_bf16(s[n2], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], b0, b1);
+          mma_bf16(s[n2 + 1], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], b2, b3);
+        }
+      }
+      // mask, online softmax (rows r0 -> s[.][0..1], r1 -> s[.][2..3])
+      const int kbase = tile * KT + 2 * tq;
+      float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+      for (int n = 0; n < NK; ++n) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int key = kbase + n * 8 + e;
+          s[n][e] = key <= qpos0 ? s[n][e] * g.scale : -INFINITY;
+          s[n][2 + e] = key <= qpos1 ? s[n][2 + e] * g.scale : -INFINITY;
+          mx0 = fmaxf(mx0, s[n][e]);
+          mx1 = fmaxf(mx1, s[n][2 + e]);
+        }
+      }
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+      const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+      const float ms0 = mn0 == -INFINITY ? 0.f : mn0, ms1 = mn1 == -INFINITY ? 0.f : mn1;
+      const float c0 = expf(m0 - ms0), c1 = expf(m1 - ms1);
+      m0 = mn0;
+      m1 = mn1;
+      float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+      for (int n = 0; n < NK; ++n) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          s[n][e] = expf(s[n][e] - ms0);
+          s[n][2 + e] = expf(s[n][2 + e] - ms1);
+          ps0 += s[n][e];
+          ps1 += s[n][2 + e];
+        }
+      }
+      l0 = l0 * c0 + ps0;
+      l1 = l1 * c1 + ps1;
+#pragma unroll
+      for (int n = 0; n < ND; ++n) {
+        o[n][0] *= c0;
+        o[n][1] *= c0;
+        o[n][2] *= c1;
+        o[n][3] *= c1;
+      }
+      // O += P V  (P from the score accumulators, V via transposed ldmatrix)
+#pragma unroll
+      for (int kk = 0; kk < KT / 16; ++kk) {
+        const uint32_t a0 = pack_bf16(s[2 * kk][0], s[2 * kk][1]);
+        const uint32_t a1 = pack_bf16(s[2 * kk][2], s[2 * kk][3]);
+        const uint32_t a2 = pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+        const uint32_t a3 = pack_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+        for (int n2 = 0; n2 < ND; n2 += 2) {
+          const int key = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+          const int dim = n2 * 8 + (lane >> 4) * 8;
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4_t(smem_u32(Vt + key * LD + dim), b0, b1, b2, b3);
+          mma_bf16(o[n2], a0, a1, a2, a3, b0, b1);
+          mma_bf16(o[n2 + 1], a0, a1, a2, a3, b2, b3);
+        }
+      }
+    }
+    __syncthreads();
+  }
+  if (!warp_active) return;
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f, inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
+  const int hd = g.n_heads * D;
+#pragma unroll
+  for (int n = 0; n < ND; ++n) {
+    const int d = n * 8 + 2 * tq;
+    if (r0 < nrows) {
+      bf16* p = out + (size_t)(start + t0 + r0 / G) * hd + (kvh * G + r0 % G) * D + d;
+      *reinterpret_cast<__nv_bfloat162*>(p) = __floats2bfloat162_rn(o[n][0] * inv0, o[n][1] * inv0);
+    }
+    if (r1 < nrows) {
+      bf16* p = out + (size_t)(start + t0 + r1 / G) * hd + (kvh * G + r1 % G) * D + d;
+      *reinterpret_cast<__nv_bfloat162*>(p) = __floats2bfloat162_rn(o[n][2] * inv1, o[n][3] * inv1);
+    }
+  }
+}
+
+// ---------------------------------------------------------------- small step kernels
+template <typename T>
+__global__ void embed_kernel(const T* __restrict__ table, const int32_t* __restrict__ ids, int dim, int vocab,
+                             T* __restrict__ x, int* status) {
+  const int i = blockIdx.x;
+  const int id = ids[i];
+  if (id < 0 || id >= vocab) {
+    if (threadIdx.x == 0) set_status(status, kStatusBadIndex);
+    for (int j = threadIdx.x; j < dim; j += blockDim.x) x[(size_t)i * dim + j] = from_f<T>(0.f);
+    return;
+  }
+  for (int j = threadIdx.x; j < dim; j += blockDim.x) x[(size_t)i * dim + j] = table[(size_t)id * dim + j];
+}
+
+__global__ void copy_rows_kernel(const uint8_t* __restrict__ src, const int32_t* __restrict__ si, uint8_t* __restrict__ dst,
+                                 const int32_t* __restrict__ di, int row_bytes) {
+  const int i = blockIdx.x;
+  const uint8_t* s = src + (size_t)(si ? si[i] : i) * row_bytes;
+  uint8_t* d = dst + (size_t)(di ? di[i] : i) * row_bytes;
+  if ((row_bytes & 15) == 0 && ((reinterpret_cast<uintptr_t>(s) | reinterpret_cast<uintptr_t>(d)) & 15) == 0) {
+    for (int j = threadIdx.x; j < row_bytes / 16; j += blockDim.x)
+      reinterpret_cast<uint4*>(d)[j] = reinterpret_cast<const uint4*>(s)[j];
+  } else {
+    for (int j = threadIdx.x; j < row_bytes; j += blockDim.x) d[j] = s[j];
+  }
+}
+
+__global__ void gather_ids_kernel(const int32_t* __restrict__ table, const int32_t* __restrict__ idx,
+                                  int32_t* __restrict__ ids, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) ids[i] = table[idx[i]];
+}
+__global__ void scatter_ids_kernel(const int32_t* __restrict__ ids, const int32_t* __restrict__ idx,
+                                   int32_t* __restrict__ table, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) table[idx[i]] = ids[i];
+}
+
+// Greedy acceptance: first mismatch between the verified tokens and the drafts; the token at
+// that position (the correction, or the bonus token when all drafts match) becomes the
+// verifier's next input (solutions/engine.py:464-475).
+__global__ void greedy_accept_kernel(const int32_t* __restrict__ y, const int32_t* __restrict__ vinfo, int nv,
+                                     int32_t* __restrict__ seq_buf, int stride, int32_t* __restrict__ acc) {
+  const int v = blockIdx.x * blockDim.x + threadIdx.x;
+  if (v >= nv) return;
+  const int start = vinfo[3 * v], T = vinfo[3 * v + 1], slot = vinfo[3 * v + 2];
+  int32_t* sb = seq_buf + (size_t)slot * stride;
+  int a = 0;
+  while (a < T - 1 && y[start + a] == sb[a + 1]) ++a;
+  acc[v] = a;
+  sb[0] = y[start + a];
+}
+
+__global__ void keys_to_ids_kernel(const unsigned long long* __restrict__ keys, int32_t* __restrict__ ids, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) ids[i] = (int32_t)(0xFFFFFFFFu - (uint32_t)(keys[i] & 0xFFFFFFFFull));
+}
+
+// argmax over logits rows (lowest index on ties, as torch.argmax)
+template <typename T>
+__global__ void __launch_bounds__(256) argmax_rows_kernel(const T* __restrict__ logits, int vocab, int32_t* __restrict__ ids) {
+  __shared__ unsigned long long red[8];
+  const int i = blockIdx.x;
+  const T* lr = logits + (size_t)i * vocab;
+  unsigned long long best = 0;
+  for (int j = threadIdx.x; j < vocab; j += 256) {
+    const unsigned long long k = argmax_key(to_f(lr[j]), (uint32_t)j);
+    best = k > best ? k : best;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long v = __shfl_xor_sync(0xffffffffu, best, o);
+    best = v > best ? v : best;
+  }
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < 8; ++w) best = red[w] > best ? red[w] : best;
+    best = red[0] > best ? red[0] : best;
+    ids[i] = (int32_t)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFull));
+  }
+}
+
+__global__ void swiglu_f32_kernel(const float* __restrict__ gu, float* __restrict__ out, int n, int inter) {
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (size_t)n * inter) return;
+  const size_t t = i / inter, j = i - t * inter;
+  const float g = gu[t * 2 * inter + j], u = gu[t * 2 * inter + inter + j];
+  out[i] = g / (1.0f + expf(-g)) * u;
+}
+
+// fp32 CUDA-core GEMM (parity path): 64 x 64 tiles, 16-wide K steps, 4 x 4 outputs per thread.
+// Each output is a sequential fp32 sum over K, independent of the token count.
+__global__ void __launch_bounds__(256) simt_gemm_f32_kernel(int epi, const float* __restrict__ x,
+                                                            const float* __restrict__ w, const float* residual,
+                                                            float* y, int n_tok, int n_out, int K) {
+  __shared__ float As[16][68];
+  __shared__ float Bs[16][68];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int t0 = blockIdx.y * 64, o0 = blockIdx.x * 64;
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < K; k0 += 16) {
+    for (int idx = threadIdx.x; idx < 64 * 16; idx += 256) {
+      const int r = idx >> 4, kk = idx & 15;
+      const int k = k0 + kk;
+      As[kk][r] = (t0 + r < n_tok && k < K) ? x[(size_t)(t0 + r) * K + k] : 0.f;
+      Bs[kk][r] = (o0 + r < n_out && k < K) ? w[(size_t)(o0 + r) * K + k] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < 16; ++kk) {
+      float a[4], bb[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        a[i] = As[kk][ty * 4 + i];
+        bb[i] = Bs[kk][tx * 4 + i];
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], bb[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int t = t0 + ty * 4 + i;
+    if (t >= n_tok) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int o = o0 + tx * 4 + j;
+      if (o >= n_out) continue;
+      const size_t idx = (size_t)t * n_out + o;
+      y[idx] = epi == EESD_EPI_RESIDUAL ? residual[idx] + acc[i][j] : acc[i][j];
+    }
+  }
+}
+
+inline int launched() { return cudaPeekAtLastError() == cudaSuccess ? EESD_OK : EESD_ERR_CUDA; }
+
+}  // namespace
+
+int attn_item_tokens(int n_heads, int n_kv_heads) {
+  const int G = n_heads / n_kv_heads;
+  return G >= 64 ? 1 : 64 / G;   // up to 64 query rows per work item
+}
+
+int launch_rmsnorm(int dtype, const void* x, const int32_t* rows, const void* w, void* y, int n, int dim, float eps,
+                   cudaStream_t s) {
+  if (n <= 0) return EESD_OK;
+  if (dtype == EESD_BF16)
+    rmsnorm_kernel<bf16><<<n, 256, 0, s>>>((const bf16*)x, rows, (const bf16*)w, (bf16*)y, dim, eps);
+  else
+    rmsnorm_kernel<float><<<n, 256, 0, s>>>((const float*)x, rows, (const float*)w, (float*)y, dim, eps);
+  return launched();
+}
+
+int launch_rope_kv(int dtype, void* qkv, const int32_t* tok_pos, const int32_t* tok_row, int n_tok, int n_heads,
+                   int n_kv_heads, int head_dim, const float* cos, const float* sin, void* kc, void* vc, int max_batch,
+                   int max_seq, int* status, cudaStream_t s) {
+  if (n_tok <= 0) return EESD_OK;
+  if (dtype == EESD_BF16)
+    rope_kv_kernel<bf16><<<n_tok, 128, 0, s>>>((bf16*)qkv, tok_pos, tok_row, n_heads, n_kv_heads, head_dim, cos, sin,
+                                               (bf16*)kc, (bf16*)vc, max_batch, max_seq, status);
+  else
+    rope_kv_kernel<float><<<n_tok, 128, 0, s>>>((float*)qkv, tok_pos, tok_row, n_heads, n_kv_heads, head_dim, cos, sin,
+                                                (float*)kc, (float*)vc, max_batch, max_seq, status);
+  return launched();
+}
+
+int launch_attention(int dtype, const AttnGeom& g, const void* q, const void* kc, const void* vc, void* out,
+                     const int32_t* blk, const int32_t* items, int n_items, int max_ctx, int* status, cudaStream_t s) {
+  (void)max_ctx;
+  (void)status;
+  if (n_items <= 0) return EESD_OK;
+  const int it = attn_item_tokens(g.n_heads, g.n_kv_heads);
+  dim3 grid(n_items, g.n_kv_heads);
+  if (dtype == EESD_BF16) {
+    if (g.head_dim == 128) {
+      const size_t sm = (size_t)(64 + 4 * 64) * (128 + 8) * 2;
+      static bool set = false;
+      if (!set) {
+        if (cudaFuncSetAttribute(attn_bf16_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm))
+          return EESD_ERR_CUDA;
+        set = true;
+      }
+      attn_bf16_kernel<128><<<grid, 128, sm, s>>>(g, it, (const bf16*)q, (const bf16*)kc, (const bf16*)vc, (bf16*)out,
+                                                  blk, items);
+    } else if (g.head_dim == 64) {
+      const size_t sm = (size_t)(64 + 4 * 64) * (64 + 8) * 2;
+      static bool set = false;
+      if (!set) {
+        if (cudaFuncSetAttribute(attn_bf16_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm))
+          return EESD_ERR_CUDA;
+        set = true;
+      }
+      attn_bf16_kernel<64><<<grid, 128, sm, s>>>(g, it, (const bf16*)q, (const bf16*)kc, (const bf16*)vc, (bf16*)out,
+                                                 blk, items);
+    } else {
+      return EESD_ERR_ARG;
+    }
+  } else {
+    if (g.head_dim == 128) {
+      const size_t sm = (size_t)(64 * 128 + 32 * 129 + 32 * 128) * 4;
+      static bool set = false;
+      if (!set) {
+        if (cudaFuncSetAttribute(attn_f32_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm))
+          return EESD_ERR_CUDA;
+        set = true;
+      }
+      attn_f32_kernel<128><<<grid, 128, sm, s>>>(g, it, (const float*)q, (const float*)kc, (const float*)vc,
+                                                 (float*)out, blk, items);
+    } else if (g.head_dim == 64) {
+      const size_t sm = (size_t)(64 * 64 + 32 * 65 + 32 * 64) * 4;
+      attn_f32_kernel<64><<<grid, 128, sm, s>>>(g, it, (const float*)q, (const float*)kc, (const float*)vc, (float*)out,
+                                                blk, items);
+    } else {
+      return EESD_ERR_ARG;
+    }
+  }
+  return launched();
+}
+
+int launch_embed(int dtype, const void* table, const int32_t* ids, int n, int dim, int vocab, void* x, int* status,
+                 cudaStream_t s) {
+  if (n <= 0) return EESD_OK;
+  if (dtype == EESD_BF16)
+    embed_kernel<bf16><<<n, 256, 0, s>>>((const bf16*)table, ids, dim, vocab, (bf16*)x, status);
+  else
+    embed_kernel<float><<<n, 256, 0, s>>>((const float*)table, ids, dim, vocab, (float*)x, status);
+  return launched();
+}
+
+int launch_copy_rows(int dtype, const void* src, const int32_t* src_idx, void* dst, const int32_t* dst_idx, int n,
+                     int width, cudaStream_t s) {
+  if (n <= 0) return EESD_OK;
+  const int eb = dtype == EESD_BF16 ? 2 : 4;
+  copy_rows_kernel<<<n, 128, 0, s>>>((const uint8_t*)src, src_idx, (uint8_t*)dst, dst_idx, width * eb);
+  return launched();
+}
+
+int launch_gather_ids(const int32_t* table, const int32_t* idx, int32_t* ids, int n, cudaStream_t s) {
+  if (n <= 0) return EESD_OK;
+  gather_ids_kernel<<<(n + 255) / 256, 256, 0, s>>>(table, idx, ids, n);
+  return launched();
+}
+int launch_scatter_ids(const int32_t* ids, const int32_t* idx, int32_t* table, int n, cudaStream_t s) {
+  if (n <= 0) return EESD_OK;
+  scatter_ids_kernel<<<(n + 255) / 256, 256, 0, s>>>(ids, idx, table, n);
+  return launched();
+}
+int launch_greedy_accept(const int32_t* y, const int32_t* vinfo, int nv, int32_t* seq_buf, int stride, int32_t* acc,
+                         cudaStream_t s) {
+  if (nv <= 0) return EESD_OK;
+  greedy_accept_kernel<<<(nv + 127) / 128, 128, 0, s>>>(y, vinfo, nv, seq_buf, stride, acc);
+  return launched();
+}
+int launch_keys_to_ids(const unsigned long long* keys, int32_t* ids, int n, cudaStream_t s) {
+  if (n <= 0) return EESD_OK;
+  keys_to_ids_kernel<<<(n + 255) / 256, 256, 0, s>>>(keys, ids, n);
+  return launched();
+}
+int launch_argmax_rows(int dtype, const void* logits, int n, int vocab, int32_t* ids, cudaStream_t s) {
+  if (n <= 0) return EESD_OK;
+  if (dtype == EESD_BF16)
+    argmax_rows_kernel<bf16><<<n, 256, 0, s>>>((const bf16*)logits, vocab, ids);
+  else
+    argmax_rows_kernel<float><<<n, 256, 0, s>>>((const float*)logits, vocab, ids);
+  return launched();
+}
+int launch_swiglu_f32(const float* gu, float* out, int n, int inter, cudaStream_t s) {
+  if (n <= 0) return EESD_OK;
+  const size_t tot = (size_t)n * inter;
+  swiglu_f32_kernel<<<(unsigned)((tot + 255) / 256), 256, 0, s>>>(gu, out, n, inter);
+  return launched();
+}
+int launch_simt_gemm_f32(int epi, const float* x, const float* w, const float* residual, float* y, int n_tok, int n_out,
+                         int k, cudaStream_t s) {
+  if (n_tok <= 0) return EESD_OK;
+  dim3 grid((n_out + 63) / 64, (n_tok + 63) / 64);
+  simt_gemm_f32_kernel<<<grid, 256, 0, s>>>(epi, x, w, residual, y, n_tok, n_out, k);
+  return launched();
+}
+
+}  // namespace eesd

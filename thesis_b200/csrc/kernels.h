@@ -1,0 +1,39 @@
+// Internal launchers of the non-GEMM kernels (not part of the C ABI).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace eesd {
+
+struct AttnGeom {
+  int n_heads, n_kv_heads, head_dim;
+  int max_batch, max_seq;
+  int ld_q;          // elements between consecutive tokens' q rows (the fused qkv row)
+  float scale;       // 1 / sqrt(head_dim)
+};
+
+int attn_item_tokens(int n_heads, int n_kv_heads);
+
+int launch_rmsnorm(int dtype, const void* x, const int32_t* rows, const void* w, void* y, int n, int dim, float eps,
+                   cudaStream_t s);
+int launch_rope_kv(int dtype, void* qkv, const int32_t* tok_pos, const int32_t* tok_row, int n_tok, int n_heads,
+                   int n_kv_heads, int head_dim, const float* cos, const float* sin, void* kc, void* vc, int max_batch,
+                   int max_seq, int* status, cudaStream_t s);
+int launch_attention(int dtype, const AttnGeom& g, const void* q, const void* kc, const void* vc, void* out,
+                     const int32_t* blk, const int32_t* items, int n_items, int max_ctx, int* status, cudaStream_t s);
+int launch_embed(int dtype, const void* table, const int32_t* ids, int n, int dim, int vocab, void* x, int* status,
+                 cudaStream_t s);
+int launch_copy_rows(int dtype, const void* src, const int32_t* src_idx, void* dst, const int32_t* dst_idx, int n,
+                     int width, cudaStream_t s);
+int launch_gather_ids(const int32_t* table, const int32_t* idx, int32_t* ids, int n, cudaStream_t s);
+int launch_scatter_ids(const int32_t* ids, const int32_t* idx, int32_t* table, int n, cudaStream_t s);
+int launch_greedy_accept(const int32_t* y, const int32_t* vinfo, int nv, int32_t* seq_buf, int stride, int32_t* acc,
+                         cudaStream_t s);
+int launch_keys_to_ids(const unsigned long long* keys, int32_t* ids, int n, cudaStream_t s);
+int launch_argmax_rows(int dtype, const void* logits, int n, int vocab, int32_t* ids, cudaStream_t s);
+int launch_swiglu_f32(const float* gu, float* out, int n, int inter, cudaStream_t s);
+int launch_simt_gemm_f32(int epi, const float* x, const float* w, const float* residual, float* y, int n_tok, int n_out,
+                         int k, cudaStream_t s);
+
+}  // namespace eesd
