@@ -36,8 +36,8 @@ def test_every_declared_symbol_is_exported_and_bound(L):
 
 def test_library_metadata(L):
     assert L.eesd_version() >= 100
-    assert L.eesd_attn_item_tokens(32, 8) == 16       # 64 query rows per attention work item
-    assert L.eesd_attn_item_tokens(32, 32) == 64
+    assert L.eesd_attn_item_tokens(32, 8) == 8        # 32 query rows per attention work item
+    assert L.eesd_attn_item_tokens(32, 32) == 32
     assert L.eesd_attn_item_tokens(6, 4) == -1        # heads must be a multiple of KV heads
 
 
@@ -49,8 +49,9 @@ def test_workspace_sizes(L):
     d.intermediate, d.vocab, d.max_batch, d.max_seq, d.max_tokens = 14336, 128256, 64, 1088, 2048
     ws = L.eesd_model_workspace_bytes(C.byref(d))
     acts = 2048 * (4096 + 6144 + 4096 + 14336) * 2
-    assert acts < ws < acts + 2048 * 6144 * 4 * 4 + (1 << 22)
-    assert L.eesd_gemm_workspace_bytes(64, 6144, 4096, lib.EPI_STORE) > 256       # split-K partials
+    assert acts < ws < acts + (1 << 22)            # split-K partials never touch global memory
+    assert L.eesd_gemm_workspace_bytes(64, 6144, 4096, lib.EPI_STORE) == 256      # the status word
+    assert L.eesd_gemm_workspace_bytes(64, 512, 4096, lib.EPI_SWIGLU) == 256 + 64 * 1024 * 4
     assert L.eesd_gemm_workspace_bytes(0, 6144, 4096, lib.EPI_STORE) == 0
 
 

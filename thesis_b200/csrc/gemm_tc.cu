@@ -12,10 +12,16 @@
 // SwiGLU keeps two accumulators (gate rows o and up rows o + I) in the same TMEM lanes, so
 // silu(g) * u is formed per thread with no data exchange.
 //
+// Split-K (few output tiles, e.g. the O and W2 projections): the S CTAs that share an output
+// tile form one thread-block cluster (1 x 1 x S).  After the main loop each CTA parks its fp32
+// accumulator in its own shared memory, and CTA r of the cluster sums column slice r of the
+// tile over the S CTAs through distributed shared memory, in split order, then applies the
+// epilogue.  No partial sums touch global memory.
+//
 // Batch invariance (needed for bit-exact speculative == autoregressive output): the K range
-// of every split and the split count depend only on the weight shape, partial sums are
-// reduced in split order by the last CTA of a tile, and every token column is an
-// independent dot product.  No atomics touch values except the order-free argmax max().
+// of every split and the split count depend only on the weight shape, the split sum has a
+// fixed order, and every token column is an independent dot product (checked on hardware for
+// every MMA N).  No atomics touch values except the order-free argmax max().
 #include <algorithm>
 #include <cstdio>
 #include <mutex>
@@ -32,6 +38,9 @@ constexpr int kBK = 64;    // K per stage: 64 bf16 = one 128-byte swizzle row
 constexpr int kThreads = 192;
 constexpr uint32_t kATileBytes = kBM * kBK * 2;
 constexpr size_t kSmemBudget = 200 * 1024;
+constexpr int kRedCols = 64;               // split-K reduction chunk (token columns)
+constexpr int kRedLd = kRedCols + 1;       // padded fp32 row of the reduction buffer
+constexpr int kMaxSplits = 8;              // portable cluster size
 
 struct alignas(8) TcParams {
   int n_tok, n_out, K;
@@ -39,7 +48,7 @@ struct alignas(8) TcParams {
   int mma_n;        // N of one tcgen05.mma (multiple of 16, <= 256)
   int kb_total;     // ceil(K / 64)
   int kb_per;       // k-blocks per split
-  int splits;
+  int splits;       // = cluster size along z
   int stages;
   int up_offset;    // SwiGLU: row of the first 'up' weight
   int tmem_cols;
@@ -47,14 +56,29 @@ struct alignas(8) TcParams {
   int ld_res;
   bf16* y;
   int ld_y;
-  float* partial;   // [splits][n_tok][ld_p]
-  int ld_p;
-  int* counters;    // [tok_tiles * out_tiles], zero between launches
   unsigned long long* keys;  // argmax keys [n_tok]
   int* status;
 };
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t dsmem_addr(uint32_t local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float dsmem_ld(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
 
 template <int EPI>
 __device__ __forceinline__ void epilogue_store(const TcParams& p, int t, int row, float g, float u) {
@@ -87,7 +111,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* accb = bars + 2 * p.stages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accb + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  int* last_flag = reinterpret_cast<int*>(tmem_slot + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tok_tile = blockIdx.x, out_tile = blockIdx.y, split = blockIdx.z;
@@ -135,6 +158,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_2d(st + kNA * kATileBytes, &map_x, kx, n0, fb);
       }
     }
+    __syncwarp();
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t idesc = idesc_bf16_f32(kBM, p.mma_n);
@@ -163,99 +187,103 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (ok) tc_commit(smem_u32(accb));
     }
-  } else {
-    // ---------------- epilogue: warps 2..5 own TMEM lane quadrants (warp % 4)
-    const int q = warp & 3;
-    const int row = m0 + q * 32 + lane;
-    const bool row_ok = row < p.n_out;
-    const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16);
-    const bool ok = mbar_wait(smem_u32(accb), 0, abort_flag);
+    __syncwarp();
+  }
+
+  // ---------------- epilogue: warps 2..5 own TMEM lane quadrants (warp % 4)
+  const bool epi_warp = warp >= 2;
+  const int q = warp & 3;
+  const int row_local = q * 32 + lane;
+  const int row = m0 + row_local;
+  const bool row_ok = row < p.n_out;
+  const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16);
+  bool ok = true;
+  if (epi_warp) {
+    ok = mbar_wait(smem_u32(accb), 0, abort_flag);
     if (!ok) {
       set_status(p.status, kStatusTimeoutEpilogue);
       *abort_flag = 1;
     }
     tc_fence_after();
-    if (ok) {
-      if (p.splits == 1) {
-        if (EPI == EESD_EPI_STORE || EPI == EESD_EPI_RESIDUAL || EPI == EESD_EPI_SWIGLU) {
-          for (int c = 0; c < p.bn; c += 16) {
-            float v[16], u[16];
-            tmem_ld16(lane_base + c, v);
-            if (EPI == EESD_EPI_SWIGLU) tmem_ld16(lane_base + p.bn + c, u);
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const int t = n0 + c + j;
-              if (t < p.n_tok && row_ok) epilogue_store<EPI>(p, t, row, v[j], EPI == EESD_EPI_SWIGLU ? u[j] : 0.f);
-            }
-          }
-        } else {  // ARGMAX: logits rounded to bf16, max over this CTA's 128 rows, then atomicMax
-          unsigned long long* red = reinterpret_cast<unsigned long long*>(smem);  // stage memory is free now
-          for (int c = 0; c < p.bn; c += 16) {
-            float v[16];
-            tmem_ld16(lane_base + c, v);
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              unsigned long long key = row_ok ? argmax_key(rnd<bf16>(v[j]), (uint32_t)row) : 0ull;
-#pragma unroll
-              for (int off = 16; off > 0; off >>= 1) {
-                const unsigned long long o = __shfl_xor_sync(0xffffffffu, key, off);
-                key = o > key ? o : key;
-              }
-              if (lane == 0) red[(c + j) * 4 + q] = key;
-            }
-          }
-          epi_bar();
-          for (int c = threadIdx.x - 64; c < p.bn; c += 128) {
-            const int t = n0 + c;
-            if (t < p.n_tok) {
-              unsigned long long k = red[c * 4];
-              for (int w = 1; w < 4; ++w) k = red[c * 4 + w] > k ? red[c * 4 + w] : k;
-              atomicMax(&p.keys[t], k);
-            }
-          }
-        }
-      } else {
-        // ---------------- split-K: publish fp32 partials, the last CTA of the tile reduces in split order
-        constexpr int kParts = (EPI == EESD_EPI_SWIGLU) ? 2 : 1;
-        float* mine = p.partial + (size_t)split * p.n_tok * p.ld_p;
+  }
+
+  if (p.splits == 1) {
+    if (epi_warp && ok) {
+      if (EPI == EESD_EPI_STORE || EPI == EESD_EPI_RESIDUAL || EPI == EESD_EPI_SWIGLU) {
         for (int c = 0; c < p.bn; c += 16) {
           float v[16], u[16];
           tmem_ld16(lane_base + c, v);
-          if (kParts == 2) tmem_ld16(lane_base + p.bn + c, u);
+          if (EPI == EESD_EPI_SWIGLU) tmem_ld16(lane_base + p.bn + c, u);
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const int t = n0 + c + j;
-            if (t < p.n_tok && row_ok) {
-              mine[(size_t)t * p.ld_p + row] = v[j];
-              if (kParts == 2) mine[(size_t)t * p.ld_p + p.n_out + row] = u[j];
-            }
+            if (t < p.n_tok && row_ok) epilogue_store<EPI>(p, t, row, v[j], EPI == EESD_EPI_SWIGLU ? u[j] : 0.f);
           }
         }
-        __threadfence();
-        epi_bar();
-        if (threadIdx.x == 64) {
-          const int tile = out_tile * gridDim.x + tok_tile;
-          const int old = atomicAdd(&p.counters[tile], 1);
-          *last_flag = (old == p.splits - 1);
-          if (old == p.splits - 1) p.counters[tile] = 0;   // ready for the next launch
+      } else {  // ARGMAX: logits rounded to bf16, max over this CTA's 128 rows, then atomicMax
+        unsigned long long* red = reinterpret_cast<unsigned long long*>(smem);  // stage memory is free now
+        for (int c = 0; c < p.bn; c += 16) {
+          float v[16];
+          tmem_ld16(lane_base + c, v);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            unsigned long long key = row_ok ? argmax_key(rnd<bf16>(v[j]), (uint32_t)row) : 0ull;
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) {
+              const unsigned long long o = __shfl_xor_sync(0xffffffffu, key, off);
+              key = o > key ? o : key;
+            }
+            if (lane == 0) red[(c + j) * 4 + q] = key;
+          }
         }
         epi_bar();
-        if (*last_flag) {
-          __threadfence();
-          const int t_end = min(p.n_tok, n0 + p.bn);
-          if (row_ok) {
-            for (int t = n0; t < t_end; ++t) {
-              float g = 0.f, u = 0.f;
-              for (int s = 0; s < p.splits; ++s) {
-                const float* ps = p.partial + ((size_t)s * p.n_tok + t) * p.ld_p;
-                g += __ldcg(ps + row);
-                if (kParts == 2) u += __ldcg(ps + p.n_out + row);
-              }
-              epilogue_store<EPI>(p, t, row, g, u);
-            }
+        for (int c = threadIdx.x - 64; c < p.bn; c += 128) {
+          const int t = n0 + c;
+          if (t < p.n_tok) {
+            unsigned long long k = red[c * 4];
+            for (int w = 1; w < 4; ++w) k = red[c * 4 + w] > k ? red[c * 4 + w] : k;
+            atomicMax(&p.keys[t], k);
           }
         }
       }
+    }
+  } else {
+    // ---------------- split-K through distributed shared memory (all threads take every barrier)
+    constexpr int kParts = (EPI == EESD_EPI_SWIGLU) ? 2 : 1;
+    float* red = reinterpret_cast<float*>(smem);                  // [kParts][128][kRedLd]
+    const uint32_t red_u32 = smem_u32(red);
+    const uint32_t rank = cluster_rank();
+    for (int c0 = 0; c0 < p.bn; c0 += kRedCols) {
+      const int cw = min(kRedCols, p.bn - c0);
+      if (epi_warp && ok) {
+        for (int cc = 0; cc < cw; cc += 16) {
+          float v[16];
+          tmem_ld16(lane_base + c0 + cc, v);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) red[row_local * kRedLd + cc + j] = v[j];
+          if (kParts == 2) {
+            tmem_ld16(lane_base + p.bn + c0 + cc, v);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) red[(128 + row_local) * kRedLd + cc + j] = v[j];
+          }
+        }
+      }
+      cluster_sync();
+      if (epi_warp && ok) {
+        const int sl = (cw + p.splits - 1) / p.splits;
+        const int lo = rank * sl, hi = min(cw, lo + sl);
+        for (int c = lo; c < hi; ++c) {
+          float g = 0.f, u = 0.f;
+          for (int s = 0; s < p.splits; ++s) {
+            const uint32_t base = dsmem_addr(red_u32, (uint32_t)s);
+            g += dsmem_ld(base + (uint32_t)(row_local * kRedLd + c) * 4u);
+            if (kParts == 2) u += dsmem_ld(base + (uint32_t)((128 + row_local) * kRedLd + c) * 4u);
+          }
+          const int t = n0 + c0 + c;
+          if (t < p.n_tok && row_ok) epilogue_store<EPI>(p, t, row, g, u);
+        }
+      }
+      cluster_sync();
     }
   }
   tc_fence_before();
@@ -287,6 +315,26 @@ int ensure_smem_attr(size_t bytes) {
     set = bytes;
   }
   return EESD_OK;
+}
+
+template <int EPI>
+int launch(const TcPlan& pl, const CUtensorMap& map_w, const CUtensorMap& map_x, const TcParams& p,
+           cudaStream_t stream) {
+  int rc = ensure_smem_attr<EPI>(pl.smem);
+  if (rc) return rc;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(pl.tok_tiles, pl.out_tiles, pl.splits);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = pl.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = pl.splits;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<EPI>, map_w, map_x, p) == cudaSuccess ? EESD_OK : EESD_ERR_CUDA;
 }
 
 }  // namespace
@@ -335,9 +383,10 @@ TcPlan tc_plan(int n_tok, int n_out, int k, int epi) {
   pl.out_tiles = (n_out + kBM - 1) / kBM;
   pl.kb_total = (k + kBK - 1) / kBK;
   // split count from the weight shape only (never from n_tok): about one wave of 148 SMs at
-  // one token tile, with at least 8 k-blocks (512 of K) per split
+  // one token tile, with at least 8 k-blocks (512 of K) per split, at most one cluster (8)
   int s = 1;
-  if (epi != EESD_EPI_ARGMAX_INTERNAL) s = std::max(1, std::min(148 / std::max(pl.out_tiles, 1), pl.kb_total / 8));
+  if (epi != EESD_EPI_ARGMAX_INTERNAL)
+    s = std::max(1, std::min(std::min(148 / std::max(pl.out_tiles, 1), pl.kb_total / 8), kMaxSplits));
   pl.kb_per = (pl.kb_total + s - 1) / s;
   pl.splits = (pl.kb_total + pl.kb_per - 1) / pl.kb_per;
   const int na = epi == EESD_EPI_SWIGLU ? 2 : 1;
@@ -345,19 +394,20 @@ TcPlan tc_plan(int n_tok, int n_out, int k, int epi) {
   pl.stages = (int)std::min<size_t>(8, kSmemBudget / stage);
   pl.smem = (size_t)pl.stages * stage + 1024 + 256;
   pl.tmem_cols = next_pow2(na * pl.bn);
-  pl.ld_p = epi == EESD_EPI_SWIGLU ? 2 * n_out : n_out;
-  pl.partial_floats = pl.splits > 1 ? (size_t)pl.splits * n_tok * pl.ld_p : 0;
-  pl.counters = pl.splits > 1 ? (size_t)pl.tok_tiles * pl.out_tiles : 0;
   return pl;
 }
 
 int tc_gemm_launch(int epi, const CUtensorMap& map_w, const void* x, int n_tok, int n_out, int k, int up_offset,
-                   const void* residual, int ld_res, void* y, int ld_y, float* partial, int* counters,
-                   unsigned long long* keys, int* status, cudaStream_t stream) {
+                   const void* residual, int ld_res, void* y, int ld_y, unsigned long long* keys, int* status,
+                   cudaStream_t stream) {
   if (n_tok <= 0 || n_out <= 0 || k <= 0) return EESD_ERR_ARG;
   const TcPlan pl = tc_plan(n_tok, n_out, k, epi);
-  if (pl.splits > 1 && (!partial || !counters)) return EESD_ERR_ARG;
   if (pl.stages < 2) return EESD_ERR_ARG;
+  // the split-K reduction buffer lives in the (then idle) stage memory
+  const size_t red_bytes = (size_t)(epi == EESD_EPI_SWIGLU ? 2 : 1) * 128 * kRedLd * 4;
+  if (pl.splits > 1 && red_bytes > (size_t)pl.stages * ((epi == EESD_EPI_SWIGLU ? 2 : 1) * kATileBytes +
+                                                        (size_t)pl.bn * kBK * 2))
+    return EESD_ERR_ARG;
   CUtensorMap map_x;
   int rc = encode_kmajor_map(&map_x, x, n_tok, k, pl.bn);
   if (rc) return rc;
@@ -377,33 +427,15 @@ int tc_gemm_launch(int epi, const CUtensorMap& map_w, const void* x, int n_tok, 
   p.ld_res = ld_res;
   p.y = static_cast<bf16*>(y);
   p.ld_y = ld_y;
-  p.partial = partial;
-  p.ld_p = pl.ld_p;
-  p.counters = counters;
   p.keys = keys;
   p.status = status;
-  dim3 grid(pl.tok_tiles, pl.out_tiles, pl.splits);
   switch (epi) {
-    case EESD_EPI_STORE:
-      if ((rc = ensure_smem_attr<EESD_EPI_STORE>(pl.smem))) return rc;
-      tc_gemm_kernel<EESD_EPI_STORE><<<grid, kThreads, pl.smem, stream>>>(map_w, map_x, p);
-      break;
-    case EESD_EPI_RESIDUAL:
-      if ((rc = ensure_smem_attr<EESD_EPI_RESIDUAL>(pl.smem))) return rc;
-      tc_gemm_kernel<EESD_EPI_RESIDUAL><<<grid, kThreads, pl.smem, stream>>>(map_w, map_x, p);
-      break;
-    case EESD_EPI_SWIGLU:
-      if ((rc = ensure_smem_attr<EESD_EPI_SWIGLU>(pl.smem))) return rc;
-      tc_gemm_kernel<EESD_EPI_SWIGLU><<<grid, kThreads, pl.smem, stream>>>(map_w, map_x, p);
-      break;
-    case EESD_EPI_ARGMAX_INTERNAL:
-      if ((rc = ensure_smem_attr<EESD_EPI_ARGMAX_INTERNAL>(pl.smem))) return rc;
-      tc_gemm_kernel<EESD_EPI_ARGMAX_INTERNAL><<<grid, kThreads, pl.smem, stream>>>(map_w, map_x, p);
-      break;
-    default:
-      return EESD_ERR_ARG;
+    case EESD_EPI_STORE: return launch<EESD_EPI_STORE>(pl, map_w, map_x, p, stream);
+    case EESD_EPI_RESIDUAL: return launch<EESD_EPI_RESIDUAL>(pl, map_w, map_x, p, stream);
+    case EESD_EPI_SWIGLU: return launch<EESD_EPI_SWIGLU>(pl, map_w, map_x, p, stream);
+    case EESD_EPI_ARGMAX_INTERNAL: return launch<EESD_EPI_ARGMAX_INTERNAL>(pl, map_w, map_x, p, stream);
+    default: return EESD_ERR_ARG;
   }
-  return cudaPeekAtLastError() == cudaSuccess ? EESD_OK : EESD_ERR_CUDA;
 }
 
 }  // namespace eesd

@@ -14,8 +14,8 @@ typedef CUresult (*PFN_encodeTiled_t)(CUtensorMap*, CUtensorMapDataType, cuuint3
                                       CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 struct TcPlan {
-  int tok_tiles, out_tiles, bn, mma_n, kb_total, kb_per, splits, stages, tmem_cols, ld_p;
-  size_t smem, partial_floats, counters;
+  int tok_tiles, out_tiles, bn, mma_n, kb_total, kb_per, splits, stages, tmem_cols;
+  size_t smem;
 };
 
 PFN_encodeTiled_t tensor_map_encoder();
@@ -24,7 +24,7 @@ int encode_kmajor_map(CUtensorMap* map, const void* base, int rows, int k, int b
 TcPlan tc_plan(int n_tok, int n_out, int k, int epi);
 void tc_set_mma_n(int n);
 int tc_gemm_launch(int epi, const CUtensorMap& map_w, const void* x, int n_tok, int n_out, int k, int up_offset,
-                   const void* residual, int ld_res, void* y, int ld_y, float* partial, int* counters,
-                   unsigned long long* keys, int* status, cudaStream_t stream);
+                   const void* residual, int ld_res, void* y, int ld_y, unsigned long long* keys, int* status,
+                   cudaStream_t stream);
 
 }  // namespace eesd

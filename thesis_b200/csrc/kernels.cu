@@ -111,10 +111,10 @@ __global__ void __launch_bounds__(128) attn_f32_kernel(AttnGeom g, int item_toke
                                                        const float* __restrict__ kc, const float* __restrict__ vc,
                                                        float* __restrict__ out, const int32_t* __restrict__ blk,
                                                        const int32_t* __restrict__ items) {
-  constexpr int KT = 32, DP = D + 1, ND = D / 32, MAXR = 16;
+  constexpr int KT = 32, DP = D + 1, ND = D / 32, MAXR = 8;
   extern __shared__ float sm[];
-  float* Qs = sm;                   // [64][D]
-  float* Ks = Qs + 64 * D;          // [KT][DP]
+  float* Qs = sm;                   // [32][D]
+  float* Ks = Qs + 32 * D;          // [KT][DP]
   float* Vs = Ks + KT * DP;         // [KT][D]
   const int item = blockIdx.x, kvh = blockIdx.y;
   const int b = items[2 * item], t0 = items[2 * item + 1];
@@ -218,42 +218,46 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// Item rows <= 32 (two 16-row groups).  The 4 warps split every 64-key tile by absolute key
+// position (warp w takes keys 16w .. 16w+15 of each tile) and keep their own running max, sum
+// and output for every row; the four partial states are merged in warp order at the end.  A
+// row's arithmetic therefore depends only on its own query, its keys and the fixed key
+// partition, never on the other rows of the launch.
 template <int D>
 __global__ void __launch_bounds__(128) attn_bf16_kernel(AttnGeom g, int item_tokens, const bf16* __restrict__ q,
                                                         const bf16* __restrict__ kc, const bf16* __restrict__ vc,
                                                         bf16* __restrict__ out, const int32_t* __restrict__ blk,
                                                         const int32_t* __restrict__ items) {
   constexpr int KT = 64;              // keys per tile
+  constexpr int NS = 3;               // cp.async stages
   constexpr int LD = D + 8;           // padded row (elements): conflict-free ldmatrix
-  constexpr int NK = KT / 8;          // score n-tiles per key tile
   constexpr int ND = D / 8;           // output n-tiles
+  constexpr int CPR = D / 8;          // 16-byte chunks per row
   extern __shared__ __align__(16) uint8_t smem8[];
-  bf16* Qs = reinterpret_cast<bf16*>(smem8);           // [64][LD]
-  bf16* Ks = Qs + 64 * LD;                              // [2][KT][LD]
-  bf16* Vs = Ks + 2 * KT * LD;                          // [2][KT][LD]
+  bf16* Qs = reinterpret_cast<bf16*>(smem8);           // [32][LD]
+  bf16* Ks = Qs + 32 * LD;                              // [NS][KT][LD]
+  bf16* Vs = Ks + NS * KT * LD;                         // [NS][KT][LD]
 
   const int item = blockIdx.x, kvh = blockIdx.y;
   const int b = items[2 * item], t0 = items[2 * item + 1];
   const int start = blk[4 * b], T = blk[4 * b + 1], row = blk[4 * b + 2], pos0 = blk[4 * b + 3];
   const int G = g.n_heads / g.n_kv_heads;
   const int nt = min(item_tokens, T - t0);
-  const int nrows = nt * G;
+  const int nrows = nt * G;                             // <= 32
   const int kv_len = pos0 + t0 + nt;
   const int n_tiles = (kv_len + KT - 1) / KT;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bf16* Kb = kc + ((size_t)row * g.n_kv_heads + kvh) * g.max_seq * D;
   const bf16* Vb = vc + ((size_t)row * g.n_kv_heads + kvh) * g.max_seq * D;
 
-  // Q rows (row r = token r / G, head kvh*G + r % G); rows >= nrows are zero
-  constexpr int CPR = D / 8;   // 16-byte chunks per row
-  for (int c = threadIdx.x; c < 64 * CPR; c += 128) {
+  for (int c = threadIdx.x; c < 32 * CPR; c += 128) {
     const int r = c / CPR, cc = c - r * CPR;
     const bool in = r < nrows;
     const bf16* src = in ? q + (size_t)(start + t0 + r / G) * g.ld_q + (kvh * G + r % G) * D + cc * 8 : q;
     cp_async16(smem_u32(Qs + r * LD + cc * 8), src, in);
   }
-  auto load_tile = [&](int tile, int buf) {
-    const int k0 = tile * KT;
+  auto load_tile = [&](int tile) {
+    const int k0 = tile * KT, buf = tile % NS;
     for (int c = threadIdx.x; c < KT * CPR; c += 128) {
       const int j = c / CPR, cc = c - j * CPR;
       const bool in = k0 + j < kv_len;
@@ -262,133 +266,162 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(AttnGeom g, int item_tok
       cp_async16(smem_u32(Vs + (buf * KT + j) * LD + cc * 8), Vb + off, in);
     }
   };
-  load_tile(0, 0);
-  cp_async_commit();
+#pragma unroll
+  for (int s = 0; s < NS - 1; ++s) {
+    if (s < n_tiles) load_tile(s);
+    cp_async_commit();
+  }
 
   const int gq = lane >> 2, tq = lane & 3;
-  const int r0 = warp * 16 + gq, r1 = r0 + 8;
-  const int qpos0 = r0 < nrows ? pos0 + t0 + r0 / G : -1;
-  const int qpos1 = r1 < nrows ? pos0 + t0 + r1 / G : -1;
-  const bool warp_active = warp * 16 < nrows;
-  float o[ND][4];
+  const int n_rg = (nrows + 15) / 16;                   // 1 or 2 row groups
+  int qpos[2][2];
 #pragma unroll
-  for (int n = 0; n < ND; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
-  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-  uint32_t qa[D / 16][4];
+  for (int rg = 0; rg < 2; ++rg) {
+    const int r0 = rg * 16 + gq, r1 = r0 + 8;
+    qpos[rg][0] = r0 < nrows ? pos0 + t0 + r0 / G : -1;
+    qpos[rg][1] = r1 < nrows ? pos0 + t0 + r1 / G : -1;
+  }
+  float o[2][ND][4];
+  float m[2][2], l[2][2];
+#pragma unroll
+  for (int rg = 0; rg < 2; ++rg) {
+    m[rg][0] = m[rg][1] = -INFINITY;
+    l[rg][0] = l[rg][1] = 0.f;
+#pragma unroll
+    for (int n = 0; n < ND; ++n) o[rg][n][0] = o[rg][n][1] = o[rg][n][2] = o[rg][n][3] = 0.f;
+  }
 
   for (int tile = 0; tile < n_tiles; ++tile) {
-    const int buf = tile & 1;
-    if (tile + 1 < n_tiles) load_tile(tile + 1, buf ^ 1);
+    if (tile + NS - 1 < n_tiles) load_tile(tile + NS - 1);
     cp_async_commit();
-    cp_async_wait<1>();
+    cp_async_wait<NS - 1>();
     __syncthreads();
-    if (tile == 0 && warp_active) {
+    const bf16* Kt = Ks + (tile % NS) * KT * LD;
+    const bf16* Vt = Vs + (tile % NS) * KT * LD;
+    const int kw = warp * 16;                           // this warp's keys inside the tile
 #pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk) {
-        const bf16* p = Qs + (warp * 16 + (lane & 15)) * LD + kk * 16 + (lane >> 4) * 8;
-        ldsm_x4(smem_u32(p), qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3]);
-      }
-    }
-    if (warp_active) {
-      const bf16* Kt = Ks + buf * KT * LD;
-      const bf16* Vt = Vs + buf * KT * LD;
-      float s[NK][4];
+    for (int rg = 0; rg < 2; ++rg) {
+      if (rg < n_rg) {
+        float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
-      for (int n = 0; n < NK; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
-#pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk) {
-#pragma unroll
-        for (int n2 = 0; n2 < NK; n2 += 2) {
-          // keys n2*8 .. n2*8+15, dims kk*16 .. +15
-          const int key = n2 * 8 + (lane & 7) + ((lane >> 4) << 3);
+        for (int kk = 0; kk < D / 16; ++kk) {
+          uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+          ldsm_x4(smem_u32(Qs + (rg * 16 + (lane & 15)) * LD + kk * 16 + (lane >> 4) * 8), a0, a1, a2, a3);
+          const int key = kw + (lane & 7) + ((lane >> 4) << 3);
           const int dim = kk * 16 + ((lane >> 3) & 1) * 8;
-          uint32_t b0, b1, b2, b3;
           ldsm_x4(smem_u32(Kt + key * LD + dim), b0, b1, b2, b3);
-          mma_bf16(s[n2], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], b0, b1);
-          mma_bf16(s[n2 + 1], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], b2, b3);
+          mma_bf16(s[0], a0, a1, a2, a3, b0, b1);
+          mma_bf16(s[1], a0, a1, a2, a3, b2, b3);
         }
-      }
-      // mask, online softmax (rows r0 -> s[.][0..1], r1 -> s[.][2..3])
-      const int kbase = tile * KT + 2 * tq;
-      float mx0 = -INFINITY, mx1 = -INFINITY;
+        const int kbase = tile * KT + kw + 2 * tq;
+        float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
-      for (int n = 0; n < NK; ++n) {
+        for (int n = 0; n < 2; ++n) {
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int key = kbase + n * 8 + e;
-          s[n][e] = key <= qpos0 ? s[n][e] * g.scale : -INFINITY;
-          s[n][2 + e] = key <= qpos1 ? s[n][2 + e] * g.scale : -INFINITY;
-          mx0 = fmaxf(mx0, s[n][e]);
-          mx1 = fmaxf(mx1, s[n][2 + e]);
+          for (int e = 0; e < 2; ++e) {
+            const int key = kbase + n * 8 + e;
+            s[n][e] = key <= qpos[rg][0] ? s[n][e] * g.scale : -INFINITY;
+            s[n][2 + e] = key <= qpos[rg][1] ? s[n][2 + e] * g.scale : -INFINITY;
+            mx0 = fmaxf(mx0, s[n][e]);
+            mx1 = fmaxf(mx1, s[n][2 + e]);
+          }
         }
-      }
-      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-      const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-      const float ms0 = mn0 == -INFINITY ? 0.f : mn0, ms1 = mn1 == -INFINITY ? 0.f : mn1;
-      const float c0 = expf(m0 - ms0), c1 = expf(m1 - ms1);
-      m0 = mn0;
-      m1 = mn1;
-      float ps0 = 0.f, ps1 = 0.f;
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+        const float mn0 = fmaxf(m[rg][0], mx0), mn1 = fmaxf(m[rg][1], mx1);
+        const float ms0 = mn0 == -INFINITY ? 0.f : mn0, ms1 = mn1 == -INFINITY ? 0.f : mn1;
+        const float c0 = expf(m[rg][0] - ms0), c1 = expf(m[rg][1] - ms1);
+        m[rg][0] = mn0;
+        m[rg][1] = mn1;
+        float ps0 = 0.f, ps1 = 0.f;
 #pragma unroll
-      for (int n = 0; n < NK; ++n) {
+        for (int n = 0; n < 2; ++n) {
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          s[n][e] = expf(s[n][e] - ms0);
-          s[n][2 + e] = expf(s[n][2 + e] - ms1);
-          ps0 += s[n][e];
-          ps1 += s[n][2 + e];
+          for (int e = 0; e < 2; ++e) {
+            s[n][e] = expf(s[n][e] - ms0);
+            s[n][2 + e] = expf(s[n][2 + e] - ms1);
+            ps0 += s[n][e];
+            ps1 += s[n][2 + e];
+          }
         }
-      }
-      l0 = l0 * c0 + ps0;
-      l1 = l1 * c1 + ps1;
-#pragma unroll
-      for (int n = 0; n < ND; ++n) {
-        o[n][0] *= c0;
-        o[n][1] *= c0;
-        o[n][2] *= c1;
-        o[n][3] *= c1;
-      }
-      // O += P V  (P from the score accumulators, V via transposed ldmatrix)
-#pragma unroll
-      for (int kk = 0; kk < KT / 16; ++kk) {
-        const uint32_t a0 = pack_bf16(s[2 * kk][0], s[2 * kk][1]);
-        const uint32_t a1 = pack_bf16(s[2 * kk][2], s[2 * kk][3]);
-        const uint32_t a2 = pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-        const uint32_t a3 = pack_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+        l[rg][0] = l[rg][0] * c0 + ps0;
+        l[rg][1] = l[rg][1] * c1 + ps1;
+        const uint32_t p0 = pack_bf16(s[0][0], s[0][1]), p1 = pack_bf16(s[0][2], s[0][3]);
+        const uint32_t p2 = pack_bf16(s[1][0], s[1][1]), p3 = pack_bf16(s[1][2], s[1][3]);
 #pragma unroll
         for (int n2 = 0; n2 < ND; n2 += 2) {
-          const int key = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+          o[rg][n2][0] *= c0;
+          o[rg][n2][1] *= c0;
+          o[rg][n2][2] *= c1;
+          o[rg][n2][3] *= c1;
+          o[rg][n2 + 1][0] *= c0;
+          o[rg][n2 + 1][1] *= c0;
+          o[rg][n2 + 1][2] *= c1;
+          o[rg][n2 + 1][3] *= c1;
+          const int key = kw + (lane & 7) + ((lane >> 3) & 1) * 8;
           const int dim = n2 * 8 + (lane >> 4) * 8;
           uint32_t b0, b1, b2, b3;
           ldsm_x4_t(smem_u32(Vt + key * LD + dim), b0, b1, b2, b3);
-          mma_bf16(o[n2], a0, a1, a2, a3, b0, b1);
-          mma_bf16(o[n2 + 1], a0, a1, a2, a3, b2, b3);
+          mma_bf16(o[rg][n2], p0, p1, p2, p3, b0, b1);
+          mma_bf16(o[rg][n2 + 1], p0, p1, p2, p3, b2, b3);
         }
       }
     }
     __syncthreads();
   }
-  if (!warp_active) return;
-  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
-  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
-  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
-  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-  const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f, inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
-  const int hd = g.n_heads * D;
+  cp_async_wait<0>();
+  __syncthreads();
+  // ---- merge the four warps' partial states in warp order (K/V stage memory is free now)
+  float* Ms = reinterpret_cast<float*>(Ks);             // [4][32]
+  float* Lw = Ms + 4 * 32;                               // [4][32]
+  float* Ow = Lw + 4 * 32;                               // [4][32][D + 4]
+  constexpr int OLD = D + 4;
 #pragma unroll
-  for (int n = 0; n < ND; ++n) {
-    const int d = n * 8 + 2 * tq;
-    if (r0 < nrows) {
-      bf16* p = out + (size_t)(start + t0 + r0 / G) * hd + (kvh * G + r0 % G) * D + d;
-      *reinterpret_cast<__nv_bfloat162*>(p) = __floats2bfloat162_rn(o[n][0] * inv0, o[n][1] * inv0);
+  for (int rg = 0; rg < 2; ++rg) {
+    if (rg < n_rg) {
+      float l0 = l[rg][0], l1 = l[rg][1];
+      l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+      l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+      l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+      l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+      const int r0 = rg * 16 + gq, r1 = r0 + 8;
+      if (tq == 0) {
+        Ms[warp * 32 + r0] = m[rg][0];
+        Ms[warp * 32 + r1] = m[rg][1];
+        Lw[warp * 32 + r0] = l0;
+        Lw[warp * 32 + r1] = l1;
+      }
+#pragma unroll
+      for (int n = 0; n < ND; ++n) {
+        const int d = n * 8 + 2 * tq;
+        Ow[(warp * 32 + r0) * OLD + d] = o[rg][n][0];
+        Ow[(warp * 32 + r0) * OLD + d + 1] = o[rg][n][1];
+        Ow[(warp * 32 + r1) * OLD + d] = o[rg][n][2];
+        Ow[(warp * 32 + r1) * OLD + d + 1] = o[rg][n][3];
+      }
     }
-    if (r1 < nrows) {
-      bf16* p = out + (size_t)(start + t0 + r1 / G) * hd + (kvh * G + r1 % G) * D + d;
-      *reinterpret_cast<__nv_bfloat162*>(p) = __floats2bfloat162_rn(o[n][2] * inv1, o[n][3] * inv1);
+  }
+  __syncthreads();
+  const int hd = g.n_heads * D;
+  for (int idx = threadIdx.x; idx < nrows * (D / 2); idx += 128) {
+    const int r = idx / (D / 2), d = (idx - r * (D / 2)) * 2;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) mx = fmaxf(mx, Ms[w * 32 + r]);
+    float lsum = 0.f, a = 0.f, bsum = 0.f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const float mw = Ms[w * 32 + r];
+      const float f = mw == -INFINITY ? 0.f : expf(mw - mx);
+      lsum += Lw[w * 32 + r] * f;
+      a += Ow[(w * 32 + r) * OLD + d] * f;
+      bsum += Ow[(w * 32 + r) * OLD + d + 1] * f;
     }
+    const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+    bf16* p = out + (size_t)(start + t0 + r / G) * hd + (kvh * G + r % G) * D + d;
+    *reinterpret_cast<__nv_bfloat162*>(p) = __floats2bfloat162_rn(a * inv, bsum * inv);
   }
 }
 
@@ -536,7 +569,7 @@ inline int launched() { return cudaPeekAtLastError() == cudaSuccess ? EESD_OK : 
 
 int attn_item_tokens(int n_heads, int n_kv_heads) {
   const int G = n_heads / n_kv_heads;
-  return G >= 64 ? 1 : 64 / G;   // up to 64 query rows per work item
+  return G >= 32 ? 1 : 32 / G;   // up to 32 query rows per work item
 }
 
 int launch_rmsnorm(int dtype, const void* x, const int32_t* rows, const void* w, void* y, int n, int dim, float eps,
@@ -571,7 +604,7 @@ int launch_attention(int dtype, const AttnGeom& g, const void* q, const void* kc
   dim3 grid(n_items, g.n_kv_heads);
   if (dtype == EESD_BF16) {
     if (g.head_dim == 128) {
-      const size_t sm = (size_t)(64 + 4 * 64) * (128 + 8) * 2;
+      const size_t sm = (size_t)(32 + 6 * 64) * (128 + 8) * 2;
       static bool set = false;
       if (!set) {
         if (cudaFuncSetAttribute(attn_bf16_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm))
@@ -581,7 +614,7 @@ int launch_attention(int dtype, const AttnGeom& g, const void* q, const void* kc
       attn_bf16_kernel<128><<<grid, 128, sm, s>>>(g, it, (const bf16*)q, (const bf16*)kc, (const bf16*)vc, (bf16*)out,
                                                   blk, items);
     } else if (g.head_dim == 64) {
-      const size_t sm = (size_t)(64 + 4 * 64) * (64 + 8) * 2;
+      const size_t sm = (size_t)(32 + 6 * 64) * (64 + 8) * 2;
       static bool set = false;
       if (!set) {
         if (cudaFuncSetAttribute(attn_bf16_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm))
@@ -595,7 +628,7 @@ int launch_attention(int dtype, const AttnGeom& g, const void* q, const void* kc
     }
   } else {
     if (g.head_dim == 128) {
-      const size_t sm = (size_t)(64 * 128 + 32 * 129 + 32 * 128) * 4;
+      const size_t sm = (size_t)(32 * 128 + 32 * 129 + 32 * 128) * 4;
       static bool set = false;
       if (!set) {
         if (cudaFuncSetAttribute(attn_f32_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm))
@@ -605,7 +638,7 @@ int launch_attention(int dtype, const AttnGeom& g, const void* q, const void* kc
       attn_f32_kernel<128><<<grid, 128, sm, s>>>(g, it, (const float*)q, (const float*)kc, (const float*)vc,
                                                  (float*)out, blk, items);
     } else if (g.head_dim == 64) {
-      const size_t sm = (size_t)(64 * 64 + 32 * 65 + 32 * 64) * 4;
+      const size_t sm = (size_t)(32 * 64 + 32 * 65 + 32 * 64) * 4;
       attn_f32_kernel<64><<<grid, 128, sm, s>>>(g, it, (const float*)q, (const float*)kc, (const float*)vc, (float*)out,
                                                 blk, items);
     } else {

@@ -65,10 +65,7 @@ struct Model {
   void *xn, *qkv, *attn, *act;
   float* gu;                    // fp32 path: [max_tokens, 2 I]
   float* logits32;              // fp32 path: [kHeadChunk, vocab]
-  float* partial;
-  int* counters;
   unsigned long long* keys;
-  size_t partial_floats, n_counters;
   int64_t launches = 0;
   bool prof = false;
   std::vector<ProfEvent> events;
@@ -79,8 +76,7 @@ struct Model {
 constexpr int kHeadChunk = 128;
 
 struct Layout {
-  size_t status, xn, qkv, attn, act, gu, logits32, partial, counters, keys, total;
-  size_t partial_floats, n_counters;
+  size_t status, xn, qkv, attn, act, gu, logits32, keys, total;
 };
 
 Layout layout_for(const EesdModelDesc& d) {
@@ -96,23 +92,6 @@ Layout layout_for(const EesdModelDesc& d) {
   L.act = c.take(T * d.intermediate * eb);
   L.gu = c.take(d.dtype == EESD_F32 ? T * 2 * d.intermediate * 4 : 0);
   L.logits32 = c.take(d.dtype == EESD_F32 ? (size_t)kHeadChunk * d.vocab * 4 : 0);
-  size_t pf = 0, nc = 0;
-  if (d.dtype == EESD_BF16) {
-    const int shapes[5][3] = {{qkv_dim, d.dim, EESD_EPI_STORE},
-                              {d.dim, q_dim, EESD_EPI_RESIDUAL},
-                              {d.intermediate, d.dim, EESD_EPI_SWIGLU},
-                              {d.dim, d.intermediate, EESD_EPI_RESIDUAL},
-                              {d.vocab, d.dim, EESD_EPI_ARGMAX_INTERNAL}};
-    for (auto& s : shapes) {
-      const TcPlan p = tc_plan(d.max_tokens, s[0], s[1], s[2]);
-      pf = std::max(pf, p.partial_floats);
-      nc = std::max(nc, p.counters);
-    }
-  }
-  L.partial_floats = pf;
-  L.n_counters = nc;
-  L.partial = c.take(pf * 4);
-  L.counters = c.take(nc * 4);
   L.keys = c.take(T * 8);
   L.total = c.off;
   return L;
@@ -144,8 +123,8 @@ int model_gemm(Model* m, int epi, const CUtensorMap& map, const void* w, const v
                int up_offset, const void* res, void* y, cudaStream_t s) {
   const EesdModelDesc& d = m->d;
   if (d.dtype == EESD_BF16) {
-    const int rc = tc_gemm_launch(epi, map, x, n_tok, n_out, k, up_offset, res, n_out, y, n_out, m->partial,
-                                  m->counters, m->keys, m->status, s);
+    const int rc = tc_gemm_launch(epi, map, x, n_tok, n_out, k, up_offset, res, n_out, y, n_out, m->keys,
+                                  m->status, s);
     m->launches += 1;
     return rc ? fail(rc, "tcgen05 gemm launch failed (n_tok=%d n_out=%d k=%d epi=%d)", n_tok, n_out, k, epi) : 0;
   }
@@ -225,11 +204,7 @@ int eesd_model_create(const EesdModelDesc* d, void** out) {
   m->act = ws + L.act;
   m->gu = reinterpret_cast<float*>(ws + L.gu);
   m->logits32 = reinterpret_cast<float*>(ws + L.logits32);
-  m->partial = reinterpret_cast<float*>(ws + L.partial);
-  m->counters = reinterpret_cast<int*>(ws + L.counters);
   m->keys = reinterpret_cast<unsigned long long*>(ws + L.keys);
-  m->partial_floats = L.partial_floats;
-  m->n_counters = L.n_counters;
   if (d->dtype == EESD_BF16) {
     m->map_qkv.resize(d->n_layers);
     m->map_o.resize(d->n_layers);
@@ -250,9 +225,8 @@ int eesd_model_create(const EesdModelDesc* d, void** out) {
       return fail(EESD_ERR_CUDA, "tensor map encode failed for the LM head");
     }
   }
-  // status and split-K tile counters start at zero (the GEMM keeps counters zero afterwards)
+  // the status word starts at zero
   cudaError_t e = cudaMemset(ws + L.status, 0, 256);
-  if (e == cudaSuccess && L.n_counters) e = cudaMemset(m->counters, 0, L.n_counters * 4);
   if (e != cudaSuccess) {
     delete m;
     return cuda_fail(e, "workspace init");
@@ -476,8 +450,7 @@ int eesd_rmsnorm(int dtype, const void* x, const int32_t* rows, const void* w, v
 
 size_t eesd_gemm_workspace_bytes(int n_tok, int n_out, int k, int epilogue) {
   if (n_tok <= 0 || n_out <= 0 || k <= 0) return 0;
-  const TcPlan p = tc_plan(n_tok, n_out, k, epilogue);
-  size_t b = 256 + align256(p.counters * 4) + align256(p.partial_floats * 4);
+  size_t b = 256;                                                                  // status word
   if (epilogue == EESD_EPI_SWIGLU) b += align256((size_t)n_tok * 2 * n_out * 4);   // fp32 path scratch
   return b;
 }
@@ -490,27 +463,23 @@ int eesd_gemm(int dtype, int epilogue, const void* x, const void* w, const void*
   const size_t need = eesd_gemm_workspace_bytes(n_tok, n_out, k, epilogue);
   if (!workspace || workspace_bytes < need) return fail(EESD_ERR_ARG, "gemm workspace %zu < %zu", workspace_bytes, need);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const TcPlan p = tc_plan(n_tok, n_out, k, epilogue);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   int* status = reinterpret_cast<int*>(ws);
-  int* counters = reinterpret_cast<int*>(ws + 256);
-  float* partial = reinterpret_cast<float*>(ws + 256 + align256(p.counters * 4));
+  if (dtype != EESD_BF16 && dtype != EESD_F32) return fail(EESD_ERR_ARG, "dtype %d", dtype);
+  cudaError_t e = cudaMemsetAsync(ws, 0, 256, s);
+  if (e != cudaSuccess) return cuda_fail(e, "gemm status reset");
   if (dtype == EESD_BF16) {
     if (k % 64) return fail(EESD_ERR_ARG, "bf16 gemm needs k %% 64 == 0");
-    cudaError_t e = cudaMemsetAsync(ws, 0, 256 + align256(p.counters * 4), s);
-    if (e != cudaSuccess) return cuda_fail(e, "gemm workspace reset");
     CUtensorMap map;
     const int rows = epilogue == EESD_EPI_SWIGLU ? up_offset + n_out : n_out;
     int rc = encode_kmajor_map(&map, w, rows, k, 128);
     if (rc) return fail(rc, "weight tensor map");
-    rc = tc_gemm_launch(epilogue, map, x, n_tok, n_out, k, up_offset, residual, n_out, y, n_out, partial, counters,
-                        nullptr, status, s);
+    rc = tc_gemm_launch(epilogue, map, x, n_tok, n_out, k, up_offset, residual, n_out, y, n_out, nullptr, status, s);
     return rc ? fail(rc, "tcgen05 gemm launch") : EESD_OK;
   }
-  if (dtype != EESD_F32) return fail(EESD_ERR_ARG, "dtype %d", dtype);
   int rc;
   if (epilogue == EESD_EPI_SWIGLU) {
-    float* gu = reinterpret_cast<float*>(ws + 256 + align256(p.counters * 4) + align256(p.partial_floats * 4));
+    float* gu = reinterpret_cast<float*>(ws + 256);
     if (up_offset != n_out) return fail(EESD_ERR_ARG, "fp32 swiglu needs up_offset == n_out");
     rc = launch_simt_gemm_f32(EESD_EPI_STORE, (const float*)x, (const float*)w, nullptr, gu, n_tok, 2 * n_out, k, s);
     if (!rc) rc = launch_swiglu_f32(gu, (float*)y, n_tok, n_out, s);
