@@ -175,6 +175,20 @@ int eesd_gemm(int dtype, int epilogue, const void* x, const void* w, const void*
 #define EESD_OPT_MMA_N 1
 int eesd_set_option(int option, int value);
 
+/* Exit head that allocates nothing, for callers that cannot call cudaMalloc (a serving
+ * runtime whose allocator is locked on its decode path, code inside a foreign stream capture, a
+ * plug-in that only receives input/output pointers).  No counterpart in the reference: it is the
+ * same computation as eesd_head_argmax (final RMSNorm with norm_w, LM head, greedy argmax of rows
+ * `rows` (nullable = 0..n-1) of x [*, dim] bf16 -> out_ids [n] int32) without a model handle or
+ * workspace.  Its scratch is a fixed 2 MiB + 1280 B __device__ array inside the library, held by
+ * every GPU that loads the library until exit.  Limits: bf16, 1 <= n <= 128, dim a multiple of
+ * 64 up to 8192; larger sizes return EESD_ERR_ARG with a message.  The first call on a device
+ * resolves the array's device address (cudaGetSymbolAddress) and should come before any stream
+ * capture.  All calls share the array: calls that overlap on the GPU race and must be serialised
+ * by the caller. */
+int eesd_head_argmax_static(const void* x, const int32_t* rows, int n, int dim, int vocab, const void* norm_w,
+                            const void* lm_head, float eps, int32_t* out_ids, void* stream);
+
 /* Device status word helpers for the primitive kernels (a caller-owned int32). */
 int eesd_status_read(const int32_t* status, int* bits_out, void* stream);
 

@@ -19,7 +19,7 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "_lib" / "libeesd.so"
-SOURCES = ["gemm_tc.cu", "kernels.cu", "runtime.cu"]
+SOURCES = ["gemm_tc.cu", "kernels.cu", "runtime.cu", "head_static.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

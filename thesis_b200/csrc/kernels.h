@@ -14,6 +14,8 @@ struct AttnGeom {
 };
 
 int attn_item_tokens(int n_heads, int n_kv_heads);
+// record the text eesd_last_error() returns for the calling thread
+void set_last_error(const char* msg);
 
 int launch_rmsnorm(int dtype, const void* x, const int32_t* rows, const void* w, void* y, int n, int dim, float eps,
                    cudaStream_t s);

@@ -151,6 +151,9 @@ int check_batch(const Model* m, const EesdBatch* b) {
 }
 
 }  // namespace
+
+void set_last_error(const char* msg) { g_err = msg; }
+
 }  // namespace eesd
 
 using namespace eesd;

@@ -62,6 +62,7 @@ SIGNATURES = {
     "eesd_gemm": (C.c_int, [C.c_int, C.c_int, vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, vp, sz, vp]),
     "eesd_set_option": (C.c_int, [C.c_int, C.c_int]),
     "eesd_status_read": (C.c_int, [vp, C.POINTER(C.c_int), vp]),
+    "eesd_head_argmax_static": (C.c_int, [vp, vp, C.c_int, C.c_int, C.c_int, vp, vp, C.c_float, vp, vp]),
 }
 
 _lib = None
