@@ -70,6 +70,8 @@ typedef struct EesdModelDesc {
   int32_t max_batch;             /* KV-cache rows */
   int32_t max_seq;               /* positions per row (multiple of 64) */
   int32_t max_tokens;            /* largest packed token count of one call */
+  int32_t weights_packed;        /* bf16 only: 1 = wqkv, wo, w13, w2 and lm_head point to tile-packed
+                                    copies (eesd_pack_weight), read as contiguous 16 KB tiles */
   /* per-layer weights: arrays (host memory) of n_layers device pointers */
   const void* const* wqkv;       /* [(Hq + 2 Hkv) D, dim] rows = [q; k; v] (common/model.py:262-263) */
   const void* const* wo;         /* [dim, Hq D] */
@@ -99,6 +101,14 @@ typedef struct EesdBatch {
   const int32_t* blk;            /* [n_blocks, 4] = (start, T, row, pos0) */
   const int32_t* items;          /* [n_items, 2] = (block, first token within block) */
 } EesdBatch;
+
+/* Tile-packed weight layout for the bf16 GEMMs: a [rows, k] row-major bf16 matrix (k % 64 == 0)
+ * becomes [ceil(rows/128) * k/64][128][64]: the 128 x 64 operand tile (row tile m, k-block j) is
+ * the contiguous 16 KB block m * (k/64) + j, so each CTA streams its weights sequentially from HBM
+ * (rows past the end are zero).  Layout change only; the GEMM numerics are unchanged.  w13 needs
+ * intermediate % 128 == 0 to be packed as one matrix. */
+size_t eesd_packed_weight_bytes(int rows, int k);
+int eesd_pack_weight(const void* w, int rows, int k, void* out, void* stream);
 
 /* Query tokens per attention work item for a model (items tile every block by this). */
 int eesd_attn_item_tokens(int n_heads, int n_kv_heads);
@@ -171,8 +181,13 @@ int eesd_gemm(int dtype, int epilogue, const void* x, const void* w, const void*
               int n_out, int k, int up_offset, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Tuning knobs.  EESD_OPT_MMA_N: N of one tcgen05.mma in the bf16 GEMM (0 = the whole token
- * tile, else a fixed multiple of 16 up to 256); numerics-neutral by design. */
+ * tile, else a fixed multiple of 16 up to 256); numerics-neutral by design.  EESD_OPT_SPLITS:
+ * split-K count (0 = derived from the weight shape; any fixed value keeps batch invariance but
+ * changes the summation order, so AR and speculative runs must use the same value).
+ * EESD_OPT_STAGES: TMA pipeline depth (0 = as many stages as fit; numerics-neutral). */
 #define EESD_OPT_MMA_N 1
+#define EESD_OPT_SPLITS 2
+#define EESD_OPT_STAGES 3
 int eesd_set_option(int option, int value);
 
 /* Exit head that allocates nothing, for callers that cannot call cudaMalloc (a serving

@@ -111,3 +111,17 @@ def test_greedy_accept(cuda_dev):
              lib.stream_ptr())
     assert acc.tolist() == [2, 4, 0]
     assert seq[:, 0].tolist() == [0, 11, 2]
+
+
+@pytest.mark.parametrize("rows,k", [(300, 512), (6144, 4096)])
+def test_pack_weight_layout(cuda_dev, rows, k):
+    """Tile-packed weights: tile (m, j) = rows 128m.. x cols 64j.., contiguous, zero-padded."""
+    w = torch.randn(rows, k, device=cuda_dev).bfloat16()
+    n = lib.load().eesd_packed_weight_bytes(rows, k)
+    out = torch.empty(n // 2, dtype=torch.bfloat16, device=cuda_dev)
+    lib.call("eesd_pack_weight", w.data_ptr(), rows, k, out.data_ptr(), lib.stream_ptr())
+    mt, kb = -(-rows // 128), k // 64
+    wp = torch.zeros(mt * 128, k, dtype=torch.bfloat16, device=cuda_dev)
+    wp[:rows] = w
+    ref = wp.view(mt, 128, kb, 64).permute(0, 2, 1, 3).reshape(-1)
+    assert torch.equal(out, ref)

@@ -8,7 +8,10 @@
 // swizzle, staged by TMA; the fp32 accumulator lives in TMEM (128 lanes x N columns).
 //   warp 0      TMA producer (one elected lane), STAGES-deep ring of (W tile, X tile)
 //   warp 1      TMEM allocator + MMA issuer (one lane), tcgen05.commit frees a stage
-//   warps 2..5  epilogue: tcgen05.ld of their 32-lane quadrant, fused epilogue, stores
+//   warps 2..9  epilogue: two warps per 32-lane TMEM quadrant (warp % 4), alternating 16-column
+//               chunks; tcgen05.ld, fused epilogue, stores
+// Token tiles are up to 256 tokens for SwiGLU (two accumulators) and 384 otherwise; a tile wider
+// than 256 is fed by two TMA boxes and two MMAs per k-step.
 // SwiGLU keeps two accumulators (gate rows o and up rows o + I) in the same TMEM lanes, so
 // silu(g) * u is formed per thread with no data exchange.
 //
@@ -35,16 +38,18 @@ namespace {
 
 constexpr int kBM = 128;   // output features per CTA (MMA M)
 constexpr int kBK = 64;    // K per stage: 64 bf16 = one 128-byte swizzle row
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
+constexpr int kEpiThreads = 256;           // warps 2..9
 constexpr uint32_t kATileBytes = kBM * kBK * 2;
-constexpr size_t kSmemBudget = 200 * 1024;
+constexpr size_t kSmemBudget = 224 * 1024;
 constexpr int kRedCols = 64;               // split-K reduction chunk (token columns)
-constexpr int kRedLd = kRedCols + 1;       // padded fp32 row of the reduction buffer
+constexpr int kRedGroups = kRedCols / 4;   // float4 groups per row; group g of row r sits at g ^ (r & 15)
 constexpr int kMaxSplits = 8;              // portable cluster size
 
 struct alignas(8) TcParams {
   int n_tok, n_out, K;
   int bn;           // token tile (multiple of mma_n)
+  int b_boxes;      // TMA boxes per token tile (1, or 2 of bn / 2 rows)
   int mma_n;        // N of one tcgen05.mma (multiple of 16, <= 256)
   int kb_total;     // ceil(K / 64)
   int kb_per;       // k-blocks per split
@@ -52,6 +57,7 @@ struct alignas(8) TcParams {
   int stages;
   int up_offset;    // SwiGLU: row of the first 'up' weight
   int tmem_cols;
+  int a_packed;     // 1: weight in tile-packed layout (3-D map over 16 KB tiles), 0: row-major 2-D map
   const bf16* residual;
   int ld_res;
   bf16* y;
@@ -60,7 +66,7 @@ struct alignas(8) TcParams {
   int* status;
 };
 
-__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
@@ -74,26 +80,43 @@ __device__ __forceinline__ uint32_t dsmem_addr(uint32_t local, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
   return r;
 }
-__device__ __forceinline__ float dsmem_ld(uint32_t addr) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+// Plain (non-volatile) 16-byte DSMEM load: ordering against the writers comes from the cluster
+// barrier, so several loads can be in flight at once.
+__device__ __forceinline__ float4 dsmem_ld4(uint32_t addr) {
+  float4 v;
+  asm("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
   return v;
 }
 
-template <int EPI>
-__device__ __forceinline__ void epilogue_store(const TcParams& p, int t, int row, float g, float u) {
-  const size_t o = (size_t)t * p.ld_y + row;
-  if (EPI == EESD_EPI_STORE) {
-    p.y[o] = __float2bfloat16_rn(g);
-  } else if (EPI == EESD_EPI_RESIDUAL) {
-    // x + F.linear(...): the product is rounded to bf16 first, then the bf16 add rounds again
-    const float r = __bfloat162float(p.residual[(size_t)t * p.ld_res + row]);
-    p.y[o] = __float2bfloat16_rn(r + rnd<bf16>(g));
-  } else if (EPI == EESD_EPI_SWIGLU) {
-    // F.silu(g) * u in bf16: g, u rounded (F.linear output), silu rounded, product rounded
-    const float gb = rnd<bf16>(g), ub = rnd<bf16>(u);
-    const float s = rnd<bf16>(gb / (1.0f + expf(-gb)));
-    p.y[o] = __float2bfloat16_rn(s * ub);
+// silu(x) = x / (1 + exp(-x)) with the fast exponential and division (results are rounded to bf16)
+__device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+
+// Epilogue of NC consecutive token columns t0.. of one output row.  Residual values are all loaded
+// before any store (the residual may be the output buffer itself, so interleaving would serialise
+// every load behind the previous store).
+template <int EPI, int NC>
+__device__ __forceinline__ void epilogue_cols(const TcParams& p, int t0, int row, const float* g, const float* u) {
+  float r[NC];
+  if (EPI == EESD_EPI_RESIDUAL) {
+#pragma unroll
+    for (int j = 0; j < NC; ++j)
+      r[j] = (t0 + j < p.n_tok) ? __bfloat162float(p.residual[(size_t)(t0 + j) * p.ld_res + row]) : 0.f;
+  }
+#pragma unroll
+  for (int j = 0; j < NC; ++j) {
+    const int t = t0 + j;
+    if (t >= p.n_tok) break;
+    const size_t o = (size_t)t * p.ld_y + row;
+    if (EPI == EESD_EPI_STORE) {
+      p.y[o] = __float2bfloat16_rn(g[j]);
+    } else if (EPI == EESD_EPI_RESIDUAL) {
+      // x + F.linear(...): the product is rounded to bf16 first, then the bf16 add rounds again
+      p.y[o] = __float2bfloat16_rn(r[j] + rnd<bf16>(g[j]));
+    } else if (EPI == EESD_EPI_SWIGLU) {
+      // F.silu(g) * u in bf16: g, u rounded (F.linear output), silu rounded, product rounded
+      const float gb = rnd<bf16>(g[j]), ub = rnd<bf16>(u[j]);
+      p.y[o] = __float2bfloat16_rn(rnd<bf16>(silu_f(gb)) * ub);
+    }
   }
 }
 
@@ -117,6 +140,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n0 = tok_tile * p.bn, m0 = out_tile * kBM;
   const int kb_begin = split * p.kb_per;
   const int nkb = min(p.kb_total, kb_begin + p.kb_per) - kb_begin;
+  pdl_trigger();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < p.stages; ++s) {
@@ -142,9 +166,36 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      for (int i = 0; i < nkb; ++i) {
+      // Weight tiles do not depend on the previous kernel: the first stages' weight loads are issued
+      // before waiting for it (programmatic dependent launch), the activation loads after.
+      auto load_a = [&](int i, uint32_t st, uint32_t fb) {
+        const int kb = kb_begin + i;
+        if (p.a_packed) {
+          // tile (row tile, k-block) = one contiguous 16 KB block: tiles of a row tile are consecutive
+          tma_load_3d(st, &map_w, 0, 0, out_tile * p.kb_total + kb, fb);
+          if (kNA == 2) tma_load_3d(st + kATileBytes, &map_w, 0, 0, (out_tile + p.up_offset / kBM) * p.kb_total + kb, fb);
+        } else {
+          tma_load_2d(st, &map_w, kb * kBK, m0, fb);
+          if (kNA == 2) tma_load_2d(st + kATileBytes, &map_w, kb * kBK, p.up_offset + m0, fb);
+        }
+      };
+      auto load_b = [&](int i, uint32_t st, uint32_t fb) {
+        const int kx = (kb_begin + i) * kBK;
+        const uint32_t bst = st + kNA * kATileBytes;
+        tma_load_2d(bst, &map_x, kx, n0, fb);
+        if (p.b_boxes == 2) tma_load_2d(bst + (uint32_t)(p.bn / 2) * 128u, &map_x, kx, n0 + p.bn / 2, fb);
+      };
+      const int pre = min(p.stages, nkb);
+      for (int i = 0; i < pre; ++i) {
+        const uint32_t fb = smem_u32(&full[i]);
+        mbar_arrive_expect_tx(fb, stage_bytes);
+        load_a(i, smem_u32(smem + (size_t)i * stage_bytes), fb);
+      }
+      pdl_wait();
+      for (int i = 0; i < pre; ++i) load_b(i, smem_u32(smem + (size_t)i * stage_bytes), smem_u32(&full[i]));
+      for (int i = pre; i < nkb; ++i) {
         const int s = i % p.stages, r = i / p.stages;
-        if (r > 0 && !mbar_wait(smem_u32(&empty[s]), (r - 1) & 1, abort_flag)) {
+        if (!mbar_wait(smem_u32(&empty[s]), (r - 1) & 1, abort_flag)) {
           set_status(p.status, kStatusTimeoutProducer);
           *abort_flag = 1;
           break;
@@ -152,10 +203,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t fb = smem_u32(&full[s]);
         mbar_arrive_expect_tx(fb, stage_bytes);
         const uint32_t st = smem_u32(smem + (size_t)s * stage_bytes);
-        const int kx = (kb_begin + i) * kBK;
-        tma_load_2d(st, &map_w, kx, m0, fb);
-        if (kNA == 2) tma_load_2d(st + kATileBytes, &map_w, kx, p.up_offset + m0, fb);
-        tma_load_2d(st + kNA * kATileBytes, &map_x, kx, n0, fb);
+        load_a(i, st, fb);
+        load_b(i, st, fb);
       }
     }
     __syncwarp();
@@ -190,15 +239,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   }
 
-  // ---------------- epilogue: warps 2..5 own TMEM lane quadrants (warp % 4)
+  // ---------------- epilogue: warps 2..9, two per TMEM lane quadrant (warp % 4); half h takes
+  // the 16-column chunks h, h+2, h+4, ...
   const bool epi_warp = warp >= 2;
   const int q = warp & 3;
+  const int half = (warp - 2) >> 2;
   const int row_local = q * 32 + lane;
   const int row = m0 + row_local;
   const bool row_ok = row < p.n_out;
   const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16);
   bool ok = true;
   if (epi_warp) {
+    pdl_wait();
     ok = mbar_wait(smem_u32(accb), 0, abort_flag);
     if (!ok) {
       set_status(p.status, kStatusTimeoutEpilogue);
@@ -208,21 +260,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   if (p.splits == 1) {
-    if (epi_warp && ok) {
-      if (EPI == EESD_EPI_STORE || EPI == EESD_EPI_RESIDUAL || EPI == EESD_EPI_SWIGLU) {
-        for (int c = 0; c < p.bn; c += 16) {
+    if (EPI == EESD_EPI_STORE || EPI == EESD_EPI_RESIDUAL || EPI == EESD_EPI_SWIGLU) {
+      if (epi_warp && ok) {
+        for (int c = half * 16; c < p.bn; c += 32) {
           float v[16], u[16];
           tmem_ld16(lane_base + c, v);
           if (EPI == EESD_EPI_SWIGLU) tmem_ld16(lane_base + p.bn + c, u);
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int t = n0 + c + j;
-            if (t < p.n_tok && row_ok) epilogue_store<EPI>(p, t, row, v[j], EPI == EESD_EPI_SWIGLU ? u[j] : 0.f);
-          }
+          if (row_ok) epilogue_cols<EPI, 16>(p, n0 + c, row, v, u);
         }
-      } else {  // ARGMAX: logits rounded to bf16, max over this CTA's 128 rows, then atomicMax
-        unsigned long long* red = reinterpret_cast<unsigned long long*>(smem);  // stage memory is free now
-        for (int c = 0; c < p.bn; c += 16) {
+      }
+    } else {  // ARGMAX: logits rounded to bf16, max over this CTA's 128 rows, then atomicMax
+      unsigned long long* red = reinterpret_cast<unsigned long long*>(smem);  // stage memory is free now
+      if (epi_warp && ok) {
+        for (int c = half * 16; c < p.bn; c += 32) {
           float v[16];
           tmem_ld16(lane_base + c, v);
 #pragma unroll
@@ -236,8 +286,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (lane == 0) red[(c + j) * 4 + q] = key;
           }
         }
-        epi_bar();
-        for (int c = threadIdx.x - 64; c < p.bn; c += 128) {
+      }
+      if (epi_warp) epi_bar();
+      if (epi_warp && ok) {
+        for (int c = threadIdx.x - 64; c < p.bn; c += kEpiThreads) {
           const int t = n0 + c;
           if (t < p.n_tok) {
             unsigned long long k = red[c * 4];
@@ -250,37 +302,52 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ---------------- split-K through distributed shared memory (all threads take every barrier)
     constexpr int kParts = (EPI == EESD_EPI_SWIGLU) ? 2 : 1;
-    float* red = reinterpret_cast<float*>(smem);                  // [kParts][128][kRedLd]
+    float4* red = reinterpret_cast<float4*>(smem);                // [kParts][128][kRedGroups] (swizzled)
     const uint32_t red_u32 = smem_u32(red);
     const uint32_t rank = cluster_rank();
+    const int sw = row_local & 15;
     for (int c0 = 0; c0 < p.bn; c0 += kRedCols) {
       const int cw = min(kRedCols, p.bn - c0);
       if (epi_warp && ok) {
-        for (int cc = 0; cc < cw; cc += 16) {
-          float v[16];
-          tmem_ld16(lane_base + c0 + cc, v);
+        for (int cc = half * 16; cc < cw; cc += 32) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) red[row_local * kRedLd + cc + j] = v[j];
-          if (kParts == 2) {
-            tmem_ld16(lane_base + p.bn + c0 + cc, v);
+          for (int part = 0; part < kParts; ++part) {
+            float v[16];
+            tmem_ld16(lane_base + part * p.bn + c0 + cc, v);
+            float4* dst = red + (part * 128 + row_local) * kRedGroups;
 #pragma unroll
-            for (int j = 0; j < 16; ++j) red[(128 + row_local) * kRedLd + cc + j] = v[j];
+            for (int j = 0; j < 4; ++j)
+              dst[((cc >> 2) + j) ^ sw] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
           }
         }
       }
       cluster_sync();
       if (epi_warp && ok) {
-        const int sl = (cw + p.splits - 1) / p.splits;
-        const int lo = rank * sl, hi = min(cw, lo + sl);
-        for (int c = lo; c < hi; ++c) {
-          float g = 0.f, u = 0.f;
+        // this CTA reduces column groups [glo, ghi) of the chunk (halves alternate groups),
+        // summing the splits in order
+        const int ng = cw >> 2;
+        const int per = (ng + p.splits - 1) / p.splits;
+        const int glo = rank * per, ghi = min(ng, glo + per);
+        for (int gi = glo + half; gi < ghi; gi += 2) {
+          float g[4] = {0.f, 0.f, 0.f, 0.f}, u[4] = {0.f, 0.f, 0.f, 0.f};
+          const uint32_t off0 = (uint32_t)((row_local * kRedGroups + (gi ^ sw)) * 16);
+          const uint32_t off1 = (uint32_t)(((128 + row_local) * kRedGroups + (gi ^ sw)) * 16);
           for (int s = 0; s < p.splits; ++s) {
             const uint32_t base = dsmem_addr(red_u32, (uint32_t)s);
-            g += dsmem_ld(base + (uint32_t)(row_local * kRedLd + c) * 4u);
-            if (kParts == 2) u += dsmem_ld(base + (uint32_t)((128 + row_local) * kRedLd + c) * 4u);
+            const float4 a = dsmem_ld4(base + off0);
+            g[0] += a.x;
+            g[1] += a.y;
+            g[2] += a.z;
+            g[3] += a.w;
+            if (kParts == 2) {
+              const float4 b = dsmem_ld4(base + off1);
+              u[0] += b.x;
+              u[1] += b.y;
+              u[2] += b.z;
+              u[3] += b.w;
+            }
           }
-          const int t = n0 + c0 + c;
-          if (t < p.n_tok && row_ok) epilogue_store<EPI>(p, t, row, g, u);
+          if (row_ok) epilogue_cols<EPI, 4>(p, n0 + c0 + 4 * gi, row, g, u);
         }
       }
       cluster_sync();
@@ -298,6 +365,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 PFN_encodeTiled_t g_encode = nullptr;
 std::once_flag g_encode_once;
 int g_mma_n_option = 0;   // 0: one MMA spans the whole token tile
+int g_splits_option = 0;  // 0: split count from the weight shape
+int g_stages_option = 0;  // 0: as many stages as the shared-memory budget holds
 
 int next_pow2(int v) {
   int p = 32;
@@ -327,13 +396,15 @@ int launch(const TcPlan& pl, const CUtensorMap& map_w, const CUtensorMap& map_x,
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = pl.smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 1;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = pl.splits;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<EPI>, map_w, map_x, p) == cudaSuccess ? EESD_OK : EESD_ERR_CUDA;
 }
 
@@ -364,34 +435,91 @@ int encode_kmajor_map(CUtensorMap* map, const void* base, int rows, int k, int b
   return r == CUDA_SUCCESS ? EESD_OK : EESD_ERR_CUDA;
 }
 
+int encode_packed_map(CUtensorMap* map, const void* base, int rows, int k) {
+  PFN_encodeTiled_t enc = tensor_map_encoder();
+  if (!enc) return EESD_ERR_CUDA;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (k % kBK) || rows <= 0) return EESD_ERR_ARG;
+  const cuuint64_t tiles = (cuuint64_t)((rows + kBM - 1) / kBM) * (k / kBK);
+  cuuint64_t dims[3] = {(cuuint64_t)kBK, (cuuint64_t)kBM, tiles};
+  cuuint64_t strides[2] = {(cuuint64_t)kBK * 2, (cuuint64_t)kATileBytes};
+  cuuint32_t box[3] = {(cuuint32_t)kBK, (cuuint32_t)kBM, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? EESD_OK : EESD_ERR_CUDA;
+}
+
+size_t packed_weight_bytes(int rows, int k) {
+  return (size_t)((rows + kBM - 1) / kBM) * (size_t)((k + kBK - 1) / kBK) * kATileBytes;
+}
+
+namespace {
+// out[(tile * 128 + r) * 64 + c] = w[(mt * 128 + r) * k + kb * 64 + c], tile = mt * KB + kb; rows past
+// the end are zero.  One thread per 16-byte chunk: writes are contiguous, reads stride by row.
+__global__ void pack_weight_kernel(const uint4* __restrict__ w, uint4* __restrict__ out, int rows, int k, size_t n) {
+  const size_t o = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (o >= n) return;
+  const int kb_total = k / kBK;
+  const size_t tile = o >> 10;                 // 128 rows x 8 chunks per tile
+  const int r = (int)((o >> 3) & 127), c = (int)(o & 7);
+  const int mt = (int)(tile / kb_total), kb = (int)(tile % kb_total);
+  const int row = mt * kBM + r;
+  out[o] = row < rows ? w[((size_t)row * k + kb * kBK) / 8 + c] : make_uint4(0, 0, 0, 0);
+}
+}  // namespace
+
+int pack_weight(const void* w, int rows, int k, void* out, cudaStream_t s) {
+  if (!w || !out || rows <= 0 || k <= 0 || k % kBK) return EESD_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(out)) & 15) return EESD_ERR_ARG;
+  const size_t n = packed_weight_bytes(rows, k) / 16;
+  pack_weight_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(static_cast<const uint4*>(w), static_cast<uint4*>(out),
+                                                                 rows, k, n);
+  return cudaPeekAtLastError() == cudaSuccess ? EESD_OK : EESD_ERR_CUDA;
+}
+
 void tc_set_mma_n(int n) { g_mma_n_option = n; }
+void tc_set_splits(int n) { g_splits_option = n; }
+void tc_set_stages(int n) { g_stages_option = n; }
 
 TcPlan tc_plan(int n_tok, int n_out, int k, int epi) {
   TcPlan pl{};
   const int mma_fixed = g_mma_n_option;
-  pl.tok_tiles = (n_tok + 255) / 256;
+  const int max_tile = epi == EESD_EPI_SWIGLU ? 256 : 384;
+  pl.tok_tiles = (n_tok + max_tile - 1) / max_tile;
   const int per = (n_tok + pl.tok_tiles - 1) / pl.tok_tiles;
   if (mma_fixed > 0) {
     pl.mma_n = mma_fixed;
     pl.bn = (per + mma_fixed - 1) / mma_fixed * mma_fixed;
-    if (pl.bn > 256) pl.bn = 256 / mma_fixed * mma_fixed;
+    if (pl.bn > max_tile) pl.bn = max_tile / mma_fixed * mma_fixed;
+    if (pl.bn > 256 && (pl.bn / 2) % 16) pl.bn = 256 / mma_fixed * mma_fixed;
     pl.tok_tiles = (n_tok + pl.bn - 1) / pl.bn;
-  } else {
+  } else if (per <= 256) {
     pl.bn = std::max(16, (per + 15) / 16 * 16);
     pl.mma_n = pl.bn;
+  } else {
+    pl.bn = (per + 31) / 32 * 32;
+    pl.mma_n = pl.bn / 2;
   }
+  pl.b_boxes = pl.bn > 256 ? 2 : 1;
   pl.out_tiles = (n_out + kBM - 1) / kBM;
   pl.kb_total = (k + kBK - 1) / kBK;
-  // split count from the weight shape only (never from n_tok): about one wave of 148 SMs at
-  // one token tile, with at least 8 k-blocks (512 of K) per split, at most one cluster (8)
+  // split count from the weight shape only (never from n_tok): weights with fewer than ~100 row
+  // tiles are split so that about one wave of 148 SMs streams them, using 2 or 4 splits (clusters of
+  // 2 or 4 CTAs pack into every GPC; 3 leaves clusters waiting for a second wave), with at least 8
+  // k-blocks (512 of K) per split
   int s = 1;
-  if (epi != EESD_EPI_ARGMAX_INTERNAL)
-    s = std::max(1, std::min(std::min(148 / std::max(pl.out_tiles, 1), pl.kb_total / 8), kMaxSplits));
+  if (epi != EESD_EPI_ARGMAX_INTERNAL && pl.out_tiles < 100) {
+    const int cap = std::min(148 / std::max(pl.out_tiles, 1), std::min(pl.kb_total / 8, 4));
+    s = cap >= 4 ? 4 : (cap >= 2 ? 2 : 1);
+  }
+  if (g_splits_option > 0 && epi != EESD_EPI_ARGMAX_INTERNAL) s = std::min(g_splits_option, kMaxSplits);
   pl.kb_per = (pl.kb_total + s - 1) / s;
   pl.splits = (pl.kb_total + pl.kb_per - 1) / pl.kb_per;
   const int na = epi == EESD_EPI_SWIGLU ? 2 : 1;
   const size_t stage = (size_t)na * kATileBytes + (size_t)pl.bn * kBK * 2;
   pl.stages = (int)std::min<size_t>(8, kSmemBudget / stage);
+  if (g_stages_option >= 2 && (size_t)g_stages_option * stage <= kSmemBudget) pl.stages = g_stages_option;
   pl.smem = (size_t)pl.stages * stage + 1024 + 256;
   pl.tmem_cols = next_pow2(na * pl.bn);
   return pl;
@@ -399,23 +527,25 @@ TcPlan tc_plan(int n_tok, int n_out, int k, int epi) {
 
 int tc_gemm_launch(int epi, const CUtensorMap& map_w, const void* x, int n_tok, int n_out, int k, int up_offset,
                    const void* residual, int ld_res, void* y, int ld_y, unsigned long long* keys, int* status,
-                   cudaStream_t stream) {
+                   cudaStream_t stream, int a_packed) {
+  if (a_packed && (k % kBK || up_offset % kBM)) return EESD_ERR_ARG;
   if (n_tok <= 0 || n_out <= 0 || k <= 0) return EESD_ERR_ARG;
   const TcPlan pl = tc_plan(n_tok, n_out, k, epi);
   if (pl.stages < 2) return EESD_ERR_ARG;
   // the split-K reduction buffer lives in the (then idle) stage memory
-  const size_t red_bytes = (size_t)(epi == EESD_EPI_SWIGLU ? 2 : 1) * 128 * kRedLd * 4;
+  const size_t red_bytes = (size_t)(epi == EESD_EPI_SWIGLU ? 2 : 1) * 128 * kRedCols * 4;
   if (pl.splits > 1 && red_bytes > (size_t)pl.stages * ((epi == EESD_EPI_SWIGLU ? 2 : 1) * kATileBytes +
                                                         (size_t)pl.bn * kBK * 2))
     return EESD_ERR_ARG;
   CUtensorMap map_x;
-  int rc = encode_kmajor_map(&map_x, x, n_tok, k, pl.bn);
+  int rc = encode_kmajor_map(&map_x, x, n_tok, k, pl.b_boxes == 2 ? pl.bn / 2 : pl.bn);
   if (rc) return rc;
   TcParams p{};
   p.n_tok = n_tok;
   p.n_out = n_out;
   p.K = k;
   p.bn = pl.bn;
+  p.b_boxes = pl.b_boxes;
   p.mma_n = pl.mma_n;
   p.kb_total = pl.kb_total;
   p.kb_per = pl.kb_per;
@@ -423,6 +553,7 @@ int tc_gemm_launch(int epi, const CUtensorMap& map_w, const void* x, int n_tok, 
   p.stages = pl.stages;
   p.up_offset = up_offset;
   p.tmem_cols = pl.tmem_cols;
+  p.a_packed = a_packed;
   p.residual = static_cast<const bf16*>(residual);
   p.ld_res = ld_res;
   p.y = static_cast<bf16*>(y);

@@ -14,7 +14,7 @@ typedef CUresult (*PFN_encodeTiled_t)(CUtensorMap*, CUtensorMapDataType, cuuint3
                                       CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 struct TcPlan {
-  int tok_tiles, out_tiles, bn, mma_n, kb_total, kb_per, splits, stages, tmem_cols;
+  int tok_tiles, out_tiles, bn, b_boxes, mma_n, kb_total, kb_per, splits, stages, tmem_cols;
   size_t smem;
 };
 
@@ -23,8 +23,17 @@ PFN_encodeTiled_t tensor_map_encoder();
 int encode_kmajor_map(CUtensorMap* map, const void* base, int rows, int k, int box_rows);
 TcPlan tc_plan(int n_tok, int n_out, int k, int epi);
 void tc_set_mma_n(int n);
+void tc_set_splits(int n);
+void tc_set_stages(int n);
+// a_packed = 1: map_w is a tile-packed weight map (encode_packed_map), else a row-major 2-D map
 int tc_gemm_launch(int epi, const CUtensorMap& map_w, const void* x, int n_tok, int n_out, int k, int up_offset,
                    const void* residual, int ld_res, void* y, int ld_y, unsigned long long* keys, int* status,
-                   cudaStream_t stream);
+                   cudaStream_t stream, int a_packed = 0);
+// Tile-packed weight layout: [ceil(rows/128) * (k/64) tiles][128 rows][64 cols], tile = row tile *
+// (k/64) + k-block, so every 128 x 64 operand tile is one contiguous 16 KB block (rows past the
+// end zero).  3-D map: {64, 128, tiles} with one tile per box and 128-byte swizzle.
+size_t packed_weight_bytes(int rows, int k);
+int pack_weight(const void* w, int rows, int k, void* out, cudaStream_t s);
+int encode_packed_map(CUtensorMap* map, const void* base, int rows, int k);
 
 }  // namespace eesd

@@ -23,19 +23,46 @@ __device__ __forceinline__ float warp_max(float v) {
 
 // ---------------------------------------------------------------- RMSNorm (common/model.py:153-156)
 // y = w * round(x * rsqrt(mean(x^2) + eps)); the sum of squares has a fixed per-row order
-// (thread-strided partial sums, then a fixed tree), so a row's result never depends on
-// which other rows share the launch.
+// (fixed per-thread chunks, then a fixed tree), so a row's result never depends on which other
+// rows share the launch.  bf16 rows of dim <= 8 * 256 * kVec are held in registers between the
+// two passes (16-byte loads).
 template <typename T>
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const T* __restrict__ x, const int32_t* __restrict__ rows,
                                                       const T* __restrict__ w, T* __restrict__ y, int dim, float eps) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float red[8];
   const int i = blockIdx.x;
   const int src = rows ? rows[i] : i;
   const T* xr = x + (size_t)src * dim;
+  T* yr = y + (size_t)i * dim;
+  constexpr int EPV = 16 / sizeof(T);              // elements per 16-byte vector
+  constexpr int kVec = 4;                           // vectors per thread held in registers
+  const bool vec = (dim % EPV) == 0 && dim <= 256 * EPV * kVec &&
+                   ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(y)) &
+                    15) == 0;
   float ss = 0.f;
-  for (int j = threadIdx.x; j < dim; j += 256) {
-    const float v = to_f(xr[j]);
-    ss = fmaf(v, v, ss);
+  uint4 buf[kVec];
+  if (vec) {
+    const int nv = dim / EPV;
+#pragma unroll
+    for (int k = 0; k < kVec; ++k) {
+      const int vi = threadIdx.x + k * 256;
+      if (vi < nv) {
+        buf[k] = reinterpret_cast<const uint4*>(xr)[vi];
+        const T* e = reinterpret_cast<const T*>(&buf[k]);
+#pragma unroll
+        for (int j = 0; j < EPV; ++j) {
+          const float v = to_f(e[j]);
+          ss = fmaf(v, v, ss);
+        }
+      }
+    }
+  } else {
+    for (int j = threadIdx.x; j < dim; j += 256) {
+      const float v = to_f(xr[j]);
+      ss = fmaf(v, v, ss);
+    }
   }
   ss = warp_sum(ss);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
@@ -47,21 +74,41 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const T* __restrict__ x, c
   }
   __syncthreads();
   const float r = red[0];
-  T* yr = y + (size_t)i * dim;
-  for (int j = threadIdx.x; j < dim; j += 256) yr[j] = from_f<T>(to_f(w[j]) * rnd<T>(to_f(xr[j]) * r));
+  if (vec) {
+    const int nv = dim / EPV;
+#pragma unroll
+    for (int k = 0; k < kVec; ++k) {
+      const int vi = threadIdx.x + k * 256;
+      if (vi < nv) {
+        const uint4 wv = reinterpret_cast<const uint4*>(w)[vi];
+        const T* e = reinterpret_cast<const T*>(&buf[k]);
+        const T* we = reinterpret_cast<const T*>(&wv);
+        uint4 ov;
+        T* oe = reinterpret_cast<T*>(&ov);
+#pragma unroll
+        for (int j = 0; j < EPV; ++j) oe[j] = from_f<T>(to_f(we[j]) * rnd<T>(to_f(e[j]) * r));
+        reinterpret_cast<uint4*>(yr)[vi] = ov;
+      }
+    }
+  } else {
+    for (int j = threadIdx.x; j < dim; j += 256) yr[j] = from_f<T>(to_f(w[j]) * rnd<T>(to_f(xr[j]) * r));
+  }
 }
 
 // ---------------------------------------------------------------- RoPE + KV append
 // common/model.py:143-150 and solutions/packed.py:176-181: q, k rotated in the rotate-half
 // layout with cos/sin cast to the model dtype; q written back in place, k and v written into
 // the cache at (row, kv head, position).  Rollback needs no kernel: stale positions beyond a
-// row's committed length are never read.
+// row's committed length are never read.  One CTA per token; thread t owns rotation pair
+// d = t % (D/2) of heads t / (D/2), t / (D/2) + 256 / (D/2), ... so the table entries are read once.
 template <typename T>
-__global__ void __launch_bounds__(128) rope_kv_kernel(T* __restrict__ qkv, const int32_t* __restrict__ tok_pos,
+__global__ void __launch_bounds__(256) rope_kv_kernel(T* __restrict__ qkv, const int32_t* __restrict__ tok_pos,
                                                       const int32_t* __restrict__ tok_row, int n_heads,
                                                       int n_kv_heads, int D, const float* __restrict__ cosb,
                                                       const float* __restrict__ sinb, T* __restrict__ kc,
                                                       T* __restrict__ vc, int max_batch, int max_seq, int* status) {
+  pdl_trigger();
+  pdl_wait();
   const int t = blockIdx.x;
   const int pos = tok_pos[t], row = tok_row[t];
   if (pos < 0 || pos >= max_seq || row < 0 || row >= max_batch) {
@@ -71,15 +118,13 @@ __global__ void __launch_bounds__(128) rope_kv_kernel(T* __restrict__ qkv, const
   const int half = D / 2;
   const int ldq = (n_heads + 2 * n_kv_heads) * D;
   T* base = qkv + (size_t)t * ldq;
-  const float* cr = cosb + (size_t)pos * D;
-  const float* sr = sinb + (size_t)pos * D;
-  const int n_rot = (n_heads + n_kv_heads) * half;
-  for (int idx = threadIdx.x; idx < n_rot; idx += blockDim.x) {
-    const int h = idx / half, d = idx - h * half;
+  const int d = threadIdx.x % half;
+  const int h0 = threadIdx.x / half, hstep = blockDim.x / half;
+  const float c1 = rnd<T>(cosb[(size_t)pos * D + d]), c2 = rnd<T>(cosb[(size_t)pos * D + d + half]);
+  const float s1 = rnd<T>(sinb[(size_t)pos * D + d]), s2 = rnd<T>(sinb[(size_t)pos * D + d + half]);
+  for (int h = h0; h < n_heads + n_kv_heads; h += hstep) {
     T* xh = base + h * D;     // heads 0..Hq-1 are q, Hq.. are k (contiguous in the fused row)
     const float x1 = to_f(xh[d]), x2 = to_f(xh[d + half]);
-    const float c1 = rnd<T>(cr[d]), c2 = rnd<T>(cr[d + half]);
-    const float s1 = rnd<T>(sr[d]), s2 = rnd<T>(sr[d + half]);
     const T o1 = from_f<T>(rnd<T>(x1 * c1) + rnd<T>(-x2 * s1));
     const T o2 = from_f<T>(rnd<T>(x2 * c2) + rnd<T>(x1 * s2));
     if (h < n_heads) {
@@ -92,9 +137,13 @@ __global__ void __launch_bounds__(128) rope_kv_kernel(T* __restrict__ qkv, const
     }
   }
   const T* v = base + (n_heads + n_kv_heads) * D;
-  for (int idx = threadIdx.x; idx < n_kv_heads * D; idx += blockDim.x) {
-    const int h = idx / D, d = idx - h * D;
-    vc[(((size_t)row * n_kv_heads + h) * max_seq + pos) * D + d] = v[idx];
+  constexpr int EPV = 16 / sizeof(T);
+  const int nvec = n_kv_heads * D / EPV;
+  for (int idx = threadIdx.x; idx < nvec; idx += blockDim.x) {
+    const int e = idx * EPV;
+    const int h = e / D, dd = e - h * D;
+    *reinterpret_cast<uint4*>(&vc[(((size_t)row * n_kv_heads + h) * max_seq + pos) * D + dd]) =
+        reinterpret_cast<const uint4*>(v)[idx];
   }
 }
 
@@ -111,6 +160,8 @@ __global__ void __launch_bounds__(128) attn_f32_kernel(AttnGeom g, int item_toke
                                                        const float* __restrict__ kc, const float* __restrict__ vc,
                                                        float* __restrict__ out, const int32_t* __restrict__ blk,
                                                        const int32_t* __restrict__ items) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int KT = 32, DP = D + 1, ND = D / 32, MAXR = 8;
   extern __shared__ float sm[];
   float* Qs = sm;                   // [32][D]
@@ -218,25 +269,34 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
-// Item rows <= 32 (two 16-row groups).  The 4 warps split every 64-key tile by absolute key
-// position (warp w takes keys 16w .. 16w+15 of each tile) and keep their own running max, sum
-// and output for every row; the four partial states are merged in warp order at the end.  A
-// row's arithmetic therefore depends only on its own query, its keys and the fixed key
+// Item rows <= 32 (two 16-row groups).  K/V tiles of 64 keys arrive by TMA (one thread issues
+// them into a 3-stage mbarrier ring; 128-byte swizzled 64-dim halves).  The 4 warps split every
+// tile by absolute key position (warp w takes keys 16w .. 16w+15) and keep their own running
+// max, sum and output for every row; the four partial states are merged in warp order at the
+// end.  A row's arithmetic therefore depends only on its own query, its keys and the fixed key
 // partition, never on the other rows of the launch.
 template <int D>
-__global__ void __launch_bounds__(128) attn_bf16_kernel(AttnGeom g, int item_tokens, const bf16* __restrict__ q,
-                                                        const bf16* __restrict__ kc, const bf16* __restrict__ vc,
+__global__ void __launch_bounds__(128) attn_bf16_kernel(const __grid_constant__ CUtensorMap kmap,
+                                                        const __grid_constant__ CUtensorMap vmap, AttnGeom g,
+                                                        int item_tokens, int layer, const bf16* __restrict__ q,
                                                         bf16* __restrict__ out, const int32_t* __restrict__ blk,
-                                                        const int32_t* __restrict__ items) {
+                                                        const int32_t* __restrict__ items, int* status) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int KT = 64;              // keys per tile
-  constexpr int NS = 3;               // cp.async stages
-  constexpr int LD = D + 8;           // padded row (elements): conflict-free ldmatrix
+  constexpr int NS = 3;               // TMA stages
+  constexpr int HALVES = D / 64;      // 64-dim swizzled sub-tiles per K (or V) tile
+  constexpr uint32_t SUB = KT * 128;  // bytes of one sub-tile (64 keys x 128 B)
+  constexpr uint32_t STAGE = 2 * HALVES * SUB;
+  constexpr int LDQ = D + 8;          // padded Q row (elements): conflict-free ldmatrix
   constexpr int ND = D / 8;           // output n-tiles
-  constexpr int CPR = D / 8;          // 16-byte chunks per row
+  constexpr int CPR = D / 8;          // 16-byte chunks per Q row
   extern __shared__ __align__(16) uint8_t smem8[];
-  bf16* Qs = reinterpret_cast<bf16*>(smem8);           // [32][LD]
-  bf16* Ks = Qs + 32 * LD;                              // [NS][KT][LD]
-  bf16* Vs = Ks + NS * KT * LD;                         // [NS][KT][LD]
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem8) + 1023) & ~uintptr_t(1023));
+  uint8_t* stages = sm;                                            // [NS][K halves | V halves]
+  bf16* Qs = reinterpret_cast<bf16*>(sm + NS * STAGE);             // [32][LDQ]
+  uint64_t* full = reinterpret_cast<uint64_t*>(Qs + 32 * LDQ);     // [NS]
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(full + NS);
 
   const int item = blockIdx.x, kvh = blockIdx.y;
   const int b = items[2 * item], t0 = items[2 * item + 1];
@@ -247,30 +307,40 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(AttnGeom g, int item_tok
   const int kv_len = pos0 + t0 + nt;
   const int n_tiles = (kv_len + KT - 1) / KT;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const bf16* Kb = kc + ((size_t)row * g.n_kv_heads + kvh) * g.max_seq * D;
-  const bf16* Vb = vc + ((size_t)row * g.n_kv_heads + kvh) * g.max_seq * D;
+  // first cache row of this (layer, row, kv head) in the 2-D [layers*B*Hkv*S, D] view
+  const int crow = ((layer * g.max_batch + row) * g.n_kv_heads + kvh) * g.max_seq;
 
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; ++s) mbar_init(smem_u32(&full[s]), 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
   for (int c = threadIdx.x; c < 32 * CPR; c += 128) {
     const int r = c / CPR, cc = c - r * CPR;
     const bool in = r < nrows;
     const bf16* src = in ? q + (size_t)(start + t0 + r / G) * g.ld_q + (kvh * G + r % G) * D + cc * 8 : q;
-    cp_async16(smem_u32(Qs + r * LD + cc * 8), src, in);
+    cp_async16(smem_u32(Qs + r * LDQ + cc * 8), src, in);
   }
-  auto load_tile = [&](int tile) {
-    const int k0 = tile * KT, buf = tile % NS;
-    for (int c = threadIdx.x; c < KT * CPR; c += 128) {
-      const int j = c / CPR, cc = c - j * CPR;
-      const bool in = k0 + j < kv_len;
-      const size_t off = in ? (size_t)(k0 + j) * D + cc * 8 : 0;
-      cp_async16(smem_u32(Ks + (buf * KT + j) * LD + cc * 8), Kb + off, in);
-      cp_async16(smem_u32(Vs + (buf * KT + j) * LD + cc * 8), Vb + off, in);
+  cp_async_commit();
+  __syncthreads();
+  auto issue = [&](int tile) {
+    const int s = tile % NS;
+    const uint32_t fb = smem_u32(&full[s]);
+    const uint32_t dst = smem_u32(stages + s * STAGE);
+    mbar_arrive_expect_tx(fb, STAGE);
+#pragma unroll
+    for (int h = 0; h < HALVES; ++h) {
+      tma_load_2d(dst + h * SUB, &kmap, h * 64, crow + tile * KT, fb);
+      tma_load_2d(dst + (HALVES + h) * SUB, &vmap, h * 64, crow + tile * KT, fb);
     }
   };
-#pragma unroll
-  for (int s = 0; s < NS - 1; ++s) {
-    if (s < n_tiles) load_tile(s);
-    cp_async_commit();
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&kmap);
+    tma_prefetch_desc(&vmap);
+    for (int t = 0; t < NS - 1 && t < n_tiles; ++t) issue(t);
   }
+  cp_async_wait<0>();
+  __syncthreads();
 
   const int gq = lane >> 2, tq = lane & 3;
   const int n_rg = (nrows + 15) / 16;                   // 1 or 2 row groups
@@ -290,15 +360,16 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(AttnGeom g, int item_tok
 #pragma unroll
     for (int n = 0; n < ND; ++n) o[rg][n][0] = o[rg][n][1] = o[rg][n][2] = o[rg][n][3] = 0.f;
   }
+  const int kw = warp * 16;                             // this warp's keys inside every tile
 
   for (int tile = 0; tile < n_tiles; ++tile) {
-    if (tile + NS - 1 < n_tiles) load_tile(tile + NS - 1);
-    cp_async_commit();
-    cp_async_wait<NS - 1>();
-    __syncthreads();
-    const bf16* Kt = Ks + (tile % NS) * KT * LD;
-    const bf16* Vt = Vs + (tile % NS) * KT * LD;
-    const int kw = warp * 16;                           // this warp's keys inside the tile
+    if (threadIdx.x == 0 && tile + NS - 1 < n_tiles) issue(tile + NS - 1);
+    if (!mbar_wait(smem_u32(&full[tile % NS]), (tile / NS) & 1, abort_flag)) {
+      set_status(status, kStatusTimeoutMma);
+      *abort_flag = 1;
+    }
+    const uint32_t kt = smem_u32(stages + (tile % NS) * STAGE);
+    const uint32_t vt = kt + HALVES * SUB;
 #pragma unroll
     for (int rg = 0; rg < 2; ++rg) {
       if (rg < n_rg) {
@@ -306,10 +377,11 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(AttnGeom g, int item_tok
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
-          ldsm_x4(smem_u32(Qs + (rg * 16 + (lane & 15)) * LD + kk * 16 + (lane >> 4) * 8), a0, a1, a2, a3);
+          ldsm_x4(smem_u32(Qs + (rg * 16 + (lane & 15)) * LDQ + kk * 16 + (lane >> 4) * 8), a0, a1, a2, a3);
           const int key = kw + (lane & 7) + ((lane >> 4) << 3);
           const int dim = kk * 16 + ((lane >> 3) & 1) * 8;
-          ldsm_x4(smem_u32(Kt + key * LD + dim), b0, b1, b2, b3);
+          const uint32_t chunk = (uint32_t)((dim & 63) >> 3) ^ (uint32_t)(key & 7);
+          ldsm_x4(kt + (dim >> 6) * SUB + key * 128 + chunk * 16, b0, b1, b2, b3);
           mma_bf16(s[0], a0, a1, a2, a3, b0, b1);
           mma_bf16(s[1], a0, a1, a2, a3, b2, b3);
         }
@@ -332,7 +404,7 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(AttnGeom g, int item_tok
         mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
         const float mn0 = fmaxf(m[rg][0], mx0), mn1 = fmaxf(m[rg][1], mx1);
         const float ms0 = mn0 == -INFINITY ? 0.f : mn0, ms1 = mn1 == -INFINITY ? 0.f : mn1;
-        const float c0 = expf(m[rg][0] - ms0), c1 = expf(m[rg][1] - ms1);
+        const float c0 = __expf(m[rg][0] - ms0), c1 = __expf(m[rg][1] - ms1);
         m[rg][0] = mn0;
         m[rg][1] = mn1;
         float ps0 = 0.f, ps1 = 0.f;
@@ -340,8 +412,8 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(AttnGeom g, int item_tok
         for (int n = 0; n < 2; ++n) {
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
-            s[n][e] = expf(s[n][e] - ms0);
-            s[n][2 + e] = expf(s[n][2 + e] - ms1);
+            s[n][e] = __expf(s[n][e] - ms0);
+            s[n][2 + e] = __expf(s[n][2 + e] - ms1);
             ps0 += s[n][e];
             ps1 += s[n][2 + e];
           }
@@ -362,8 +434,9 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(AttnGeom g, int item_tok
           o[rg][n2 + 1][3] *= c1;
           const int key = kw + (lane & 7) + ((lane >> 3) & 1) * 8;
           const int dim = n2 * 8 + (lane >> 4) * 8;
+          const uint32_t chunk = (uint32_t)((dim & 63) >> 3) ^ (uint32_t)(key & 7);
           uint32_t b0, b1, b2, b3;
-          ldsm_x4_t(smem_u32(Vt + key * LD + dim), b0, b1, b2, b3);
+          ldsm_x4_t(vt + (dim >> 6) * SUB + key * 128 + chunk * 16, b0, b1, b2, b3);
           mma_bf16(o[rg][n2], p0, p1, p2, p3, b0, b1);
           mma_bf16(o[rg][n2 + 1], p0, p1, p2, p3, b2, b3);
         }
@@ -371,13 +444,11 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(AttnGeom g, int item_tok
     }
     __syncthreads();
   }
-  cp_async_wait<0>();
-  __syncthreads();
-  // ---- merge the four warps' partial states in warp order (K/V stage memory is free now)
-  float* Ms = reinterpret_cast<float*>(Ks);             // [4][32]
-  float* Lw = Ms + 4 * 32;                               // [4][32]
-  float* Ow = Lw + 4 * 32;                               // [4][32][D + 4]
+  // ---- merge the four warps' partial states in warp order (stage memory is free now)
   constexpr int OLD = D + 4;
+  float* Ms = reinterpret_cast<float*>(stages);          // [4][32]
+  float* Lw = Ms + 4 * 32;                               // [4][32]
+  float* Ow = Lw + 4 * 32;                               // [4][32][OLD]
 #pragma unroll
   for (int rg = 0; rg < 2; ++rg) {
     if (rg < n_rg) {
@@ -396,10 +467,8 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(AttnGeom g, int item_tok
 #pragma unroll
       for (int n = 0; n < ND; ++n) {
         const int d = n * 8 + 2 * tq;
-        Ow[(warp * 32 + r0) * OLD + d] = o[rg][n][0];
-        Ow[(warp * 32 + r0) * OLD + d + 1] = o[rg][n][1];
-        Ow[(warp * 32 + r1) * OLD + d] = o[rg][n][2];
-        Ow[(warp * 32 + r1) * OLD + d + 1] = o[rg][n][3];
+        *reinterpret_cast<float2*>(&Ow[(warp * 32 + r0) * OLD + d]) = make_float2(o[rg][n][0], o[rg][n][1]);
+        *reinterpret_cast<float2*>(&Ow[(warp * 32 + r1) * OLD + d]) = make_float2(o[rg][n][2], o[rg][n][3]);
       }
     }
   }
@@ -414,10 +483,11 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(AttnGeom g, int item_tok
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
       const float mw = Ms[w * 32 + r];
-      const float f = mw == -INFINITY ? 0.f : expf(mw - mx);
+      const float f = mw == -INFINITY ? 0.f : __expf(mw - mx);
+      const float2 ov = *reinterpret_cast<const float2*>(&Ow[(w * 32 + r) * OLD + d]);
       lsum += Lw[w * 32 + r] * f;
-      a += Ow[(w * 32 + r) * OLD + d] * f;
-      bsum += Ow[(w * 32 + r) * OLD + d + 1] * f;
+      a += ov.x * f;
+      bsum += ov.y * f;
     }
     const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
     bf16* p = out + (size_t)(start + t0 + r / G) * hd + (kvh * G + r % G) * D + d;
@@ -429,6 +499,8 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(AttnGeom g, int item_tok
 template <typename T>
 __global__ void embed_kernel(const T* __restrict__ table, const int32_t* __restrict__ ids, int dim, int vocab,
                              T* __restrict__ x, int* status) {
+  pdl_trigger();
+  pdl_wait();
   const int i = blockIdx.x;
   const int id = ids[i];
   if (id < 0 || id >= vocab) {
@@ -441,6 +513,8 @@ __global__ void embed_kernel(const T* __restrict__ table, const int32_t* __restr
 
 __global__ void copy_rows_kernel(const uint8_t* __restrict__ src, const int32_t* __restrict__ si, uint8_t* __restrict__ dst,
                                  const int32_t* __restrict__ di, int row_bytes) {
+  pdl_trigger();
+  pdl_wait();
   const int i = blockIdx.x;
   const uint8_t* s = src + (size_t)(si ? si[i] : i) * row_bytes;
   uint8_t* d = dst + (size_t)(di ? di[i] : i) * row_bytes;
@@ -454,11 +528,15 @@ __global__ void copy_rows_kernel(const uint8_t* __restrict__ src, const int32_t*
 
 __global__ void gather_ids_kernel(const int32_t* __restrict__ table, const int32_t* __restrict__ idx,
                                   int32_t* __restrict__ ids, int n) {
+  pdl_trigger();
+  pdl_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) ids[i] = table[idx[i]];
 }
 __global__ void scatter_ids_kernel(const int32_t* __restrict__ ids, const int32_t* __restrict__ idx,
                                    int32_t* __restrict__ table, int n) {
+  pdl_trigger();
+  pdl_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) table[idx[i]] = ids[i];
 }
@@ -468,6 +546,8 @@ __global__ void scatter_ids_kernel(const int32_t* __restrict__ ids, const int32_
 // verifier's next input (solutions/engine.py:464-475).
 __global__ void greedy_accept_kernel(const int32_t* __restrict__ y, const int32_t* __restrict__ vinfo, int nv,
                                      int32_t* __restrict__ seq_buf, int stride, int32_t* __restrict__ acc) {
+  pdl_trigger();
+  pdl_wait();
   const int v = blockIdx.x * blockDim.x + threadIdx.x;
   if (v >= nv) return;
   const int start = vinfo[3 * v], T = vinfo[3 * v + 1], slot = vinfo[3 * v + 2];
@@ -479,6 +559,8 @@ __global__ void greedy_accept_kernel(const int32_t* __restrict__ y, const int32_
 }
 
 __global__ void keys_to_ids_kernel(const unsigned long long* __restrict__ keys, int32_t* __restrict__ ids, int n) {
+  pdl_trigger();
+  pdl_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) ids[i] = (int32_t)(0xFFFFFFFFu - (uint32_t)(keys[i] & 0xFFFFFFFFull));
 }
@@ -486,6 +568,8 @@ __global__ void keys_to_ids_kernel(const unsigned long long* __restrict__ keys, 
 // argmax over logits rows (lowest index on ties, as torch.argmax)
 template <typename T>
 __global__ void __launch_bounds__(256) argmax_rows_kernel(const T* __restrict__ logits, int vocab, int32_t* __restrict__ ids) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ unsigned long long red[8];
   const int i = blockIdx.x;
   const T* lr = logits + (size_t)i * vocab;
@@ -509,6 +593,8 @@ __global__ void __launch_bounds__(256) argmax_rows_kernel(const T* __restrict__ 
 }
 
 __global__ void swiglu_f32_kernel(const float* __restrict__ gu, float* __restrict__ out, int n, int inter) {
+  pdl_trigger();
+  pdl_wait();
   const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (size_t)n * inter) return;
   const size_t t = i / inter, j = i - t * inter;
@@ -521,6 +607,8 @@ __global__ void swiglu_f32_kernel(const float* __restrict__ gu, float* __restric
 __global__ void __launch_bounds__(256) simt_gemm_f32_kernel(int epi, const float* __restrict__ x,
                                                             const float* __restrict__ w, const float* residual,
                                                             float* y, int n_tok, int n_out, int K) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float As[16][68];
   __shared__ float Bs[16][68];
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
@@ -576,9 +664,9 @@ int launch_rmsnorm(int dtype, const void* x, const int32_t* rows, const void* w,
                    cudaStream_t s) {
   if (n <= 0) return EESD_OK;
   if (dtype == EESD_BF16)
-    rmsnorm_kernel<bf16><<<n, 256, 0, s>>>((const bf16*)x, rows, (const bf16*)w, (bf16*)y, dim, eps);
+    launch_pdl(rmsnorm_kernel<bf16>, dim3(n), dim3(256), 0, s, (const bf16*)x, rows, (const bf16*)w, (bf16*)y, dim, eps);
   else
-    rmsnorm_kernel<float><<<n, 256, 0, s>>>((const float*)x, rows, (const float*)w, (float*)y, dim, eps);
+    launch_pdl(rmsnorm_kernel<float>, dim3(n), dim3(256), 0, s, (const float*)x, rows, (const float*)w, (float*)y, dim, eps);
   return launched();
 }
 
@@ -587,46 +675,50 @@ int launch_rope_kv(int dtype, void* qkv, const int32_t* tok_pos, const int32_t* 
                    int max_seq, int* status, cudaStream_t s) {
   if (n_tok <= 0) return EESD_OK;
   if (dtype == EESD_BF16)
-    rope_kv_kernel<bf16><<<n_tok, 128, 0, s>>>((bf16*)qkv, tok_pos, tok_row, n_heads, n_kv_heads, head_dim, cos, sin,
+    launch_pdl(rope_kv_kernel<bf16>, dim3(n_tok), dim3(256), 0, s, (bf16*)qkv, tok_pos, tok_row, n_heads, n_kv_heads, head_dim, cos, sin,
                                                (bf16*)kc, (bf16*)vc, max_batch, max_seq, status);
   else
-    rope_kv_kernel<float><<<n_tok, 128, 0, s>>>((float*)qkv, tok_pos, tok_row, n_heads, n_kv_heads, head_dim, cos, sin,
+    launch_pdl(rope_kv_kernel<float>, dim3(n_tok), dim3(256), 0, s, (float*)qkv, tok_pos, tok_row, n_heads, n_kv_heads, head_dim, cos, sin,
                                                 (float*)kc, (float*)vc, max_batch, max_seq, status);
   return launched();
 }
 
 int launch_attention(int dtype, const AttnGeom& g, const void* q, const void* kc, const void* vc, void* out,
-                     const int32_t* blk, const int32_t* items, int n_items, int max_ctx, int* status, cudaStream_t s) {
+                     const int32_t* blk, const int32_t* items, int n_items, int max_ctx, int* status, cudaStream_t s,
+                     const CUtensorMap* kmap, const CUtensorMap* vmap, int layer) {
   (void)max_ctx;
-  (void)status;
   if (n_items <= 0) return EESD_OK;
   const int it = attn_item_tokens(g.n_heads, g.n_kv_heads);
   dim3 grid(n_items, g.n_kv_heads);
   if (dtype == EESD_BF16) {
+    if (!kmap || !vmap) return EESD_ERR_ARG;
     if (g.head_dim == 128) {
-      const size_t sm = (size_t)(32 + 6 * 64) * (128 + 8) * 2;
+      const size_t sm = 1024 + 3 * (2 * 2 * 64 * 128) + 32 * (128 + 8) * 2 + 64;
       static bool set = false;
       if (!set) {
         if (cudaFuncSetAttribute(attn_bf16_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm))
           return EESD_ERR_CUDA;
         set = true;
       }
-      attn_bf16_kernel<128><<<grid, 128, sm, s>>>(g, it, (const bf16*)q, (const bf16*)kc, (const bf16*)vc, (bf16*)out,
-                                                  blk, items);
+      launch_pdl(attn_bf16_kernel<128>, dim3(grid), dim3(128), sm, s, *kmap, *vmap, g, it, layer, (const bf16*)q, (bf16*)out, blk, items,
+                                                  status);
     } else if (g.head_dim == 64) {
-      const size_t sm = (size_t)(32 + 6 * 64) * (64 + 8) * 2;
+      const size_t sm = 1024 + 3 * (2 * 1 * 64 * 128) + 32 * (64 + 8) * 2 + 64;
       static bool set = false;
       if (!set) {
         if (cudaFuncSetAttribute(attn_bf16_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm))
           return EESD_ERR_CUDA;
         set = true;
       }
-      attn_bf16_kernel<64><<<grid, 128, sm, s>>>(g, it, (const bf16*)q, (const bf16*)kc, (const bf16*)vc, (bf16*)out,
-                                                 blk, items);
+      launch_pdl(attn_bf16_kernel<64>, dim3(grid), dim3(128), sm, s, *kmap, *vmap, g, it, layer, (const bf16*)q, (bf16*)out, blk, items,
+                                                 status);
     } else {
       return EESD_ERR_ARG;
     }
   } else {
+    const size_t layer_off = (size_t)g.max_batch * g.n_kv_heads * g.max_seq * g.head_dim * (size_t)layer;
+    const float* kl = static_cast<const float*>(kc) + layer_off;
+    const float* vl = static_cast<const float*>(vc) + layer_off;
     if (g.head_dim == 128) {
       const size_t sm = (size_t)(32 * 128 + 32 * 129 + 32 * 128) * 4;
       static bool set = false;
@@ -635,12 +727,10 @@ int launch_attention(int dtype, const AttnGeom& g, const void* q, const void* kc
           return EESD_ERR_CUDA;
         set = true;
       }
-      attn_f32_kernel<128><<<grid, 128, sm, s>>>(g, it, (const float*)q, (const float*)kc, (const float*)vc,
-                                                 (float*)out, blk, items);
+      launch_pdl(attn_f32_kernel<128>, dim3(grid), dim3(128), sm, s, g, it, (const float*)q, kl, vl, (float*)out, blk, items);
     } else if (g.head_dim == 64) {
       const size_t sm = (size_t)(32 * 64 + 32 * 65 + 32 * 64) * 4;
-      attn_f32_kernel<64><<<grid, 128, sm, s>>>(g, it, (const float*)q, (const float*)kc, (const float*)vc, (float*)out,
-                                                blk, items);
+      launch_pdl(attn_f32_kernel<64>, dim3(grid), dim3(128), sm, s, g, it, (const float*)q, kl, vl, (float*)out, blk, items);
     } else {
       return EESD_ERR_ARG;
     }
@@ -652,9 +742,9 @@ int launch_embed(int dtype, const void* table, const int32_t* ids, int n, int di
                  cudaStream_t s) {
   if (n <= 0) return EESD_OK;
   if (dtype == EESD_BF16)
-    embed_kernel<bf16><<<n, 256, 0, s>>>((const bf16*)table, ids, dim, vocab, (bf16*)x, status);
+    launch_pdl(embed_kernel<bf16>, dim3(n), dim3(256), 0, s, (const bf16*)table, ids, dim, vocab, (bf16*)x, status);
   else
-    embed_kernel<float><<<n, 256, 0, s>>>((const float*)table, ids, dim, vocab, (float*)x, status);
+    launch_pdl(embed_kernel<float>, dim3(n), dim3(256), 0, s, (const float*)table, ids, dim, vocab, (float*)x, status);
   return launched();
 }
 
@@ -662,50 +752,50 @@ int launch_copy_rows(int dtype, const void* src, const int32_t* src_idx, void* d
                      int width, cudaStream_t s) {
   if (n <= 0) return EESD_OK;
   const int eb = dtype == EESD_BF16 ? 2 : 4;
-  copy_rows_kernel<<<n, 128, 0, s>>>((const uint8_t*)src, src_idx, (uint8_t*)dst, dst_idx, width * eb);
+  launch_pdl(copy_rows_kernel, dim3(n), dim3(128), 0, s, (const uint8_t*)src, src_idx, (uint8_t*)dst, dst_idx, width * eb);
   return launched();
 }
 
 int launch_gather_ids(const int32_t* table, const int32_t* idx, int32_t* ids, int n, cudaStream_t s) {
   if (n <= 0) return EESD_OK;
-  gather_ids_kernel<<<(n + 255) / 256, 256, 0, s>>>(table, idx, ids, n);
+  launch_pdl(gather_ids_kernel, dim3((n + 255) / 256), dim3(256), 0, s, table, idx, ids, n);
   return launched();
 }
 int launch_scatter_ids(const int32_t* ids, const int32_t* idx, int32_t* table, int n, cudaStream_t s) {
   if (n <= 0) return EESD_OK;
-  scatter_ids_kernel<<<(n + 255) / 256, 256, 0, s>>>(ids, idx, table, n);
+  launch_pdl(scatter_ids_kernel, dim3((n + 255) / 256), dim3(256), 0, s, ids, idx, table, n);
   return launched();
 }
 int launch_greedy_accept(const int32_t* y, const int32_t* vinfo, int nv, int32_t* seq_buf, int stride, int32_t* acc,
                          cudaStream_t s) {
   if (nv <= 0) return EESD_OK;
-  greedy_accept_kernel<<<(nv + 127) / 128, 128, 0, s>>>(y, vinfo, nv, seq_buf, stride, acc);
+  launch_pdl(greedy_accept_kernel, dim3((nv + 127) / 128), dim3(128), 0, s, y, vinfo, nv, seq_buf, stride, acc);
   return launched();
 }
 int launch_keys_to_ids(const unsigned long long* keys, int32_t* ids, int n, cudaStream_t s) {
   if (n <= 0) return EESD_OK;
-  keys_to_ids_kernel<<<(n + 255) / 256, 256, 0, s>>>(keys, ids, n);
+  launch_pdl(keys_to_ids_kernel, dim3((n + 255) / 256), dim3(256), 0, s, keys, ids, n);
   return launched();
 }
 int launch_argmax_rows(int dtype, const void* logits, int n, int vocab, int32_t* ids, cudaStream_t s) {
   if (n <= 0) return EESD_OK;
   if (dtype == EESD_BF16)
-    argmax_rows_kernel<bf16><<<n, 256, 0, s>>>((const bf16*)logits, vocab, ids);
+    launch_pdl(argmax_rows_kernel<bf16>, dim3(n), dim3(256), 0, s, (const bf16*)logits, vocab, ids);
   else
-    argmax_rows_kernel<float><<<n, 256, 0, s>>>((const float*)logits, vocab, ids);
+    launch_pdl(argmax_rows_kernel<float>, dim3(n), dim3(256), 0, s, (const float*)logits, vocab, ids);
   return launched();
 }
 int launch_swiglu_f32(const float* gu, float* out, int n, int inter, cudaStream_t s) {
   if (n <= 0) return EESD_OK;
   const size_t tot = (size_t)n * inter;
-  swiglu_f32_kernel<<<(unsigned)((tot + 255) / 256), 256, 0, s>>>(gu, out, n, inter);
+  launch_pdl(swiglu_f32_kernel, dim3((unsigned)((tot + 255) / 256)), dim3(256), 0, s, gu, out, n, inter);
   return launched();
 }
 int launch_simt_gemm_f32(int epi, const float* x, const float* w, const float* residual, float* y, int n_tok, int n_out,
                          int k, cudaStream_t s) {
   if (n_tok <= 0) return EESD_OK;
   dim3 grid((n_out + 63) / 64, (n_tok + 63) / 64);
-  simt_gemm_f32_kernel<<<grid, 256, 0, s>>>(epi, x, w, residual, y, n_tok, n_out, k);
+  launch_pdl(simt_gemm_f32_kernel, dim3(grid), dim3(256), 0, s, epi, x, w, residual, y, n_tok, n_out, k);
   return launched();
 }
 

@@ -60,6 +60,7 @@ struct Model {
   std::vector<const void*> wqkv, wo, w13, w2, attn_norm, ffn_norm;
   std::vector<CUtensorMap> map_qkv, map_o, map_13, map_2;
   CUtensorMap map_head;
+  CUtensorMap map_kc, map_vc;   // whole KV cache as [layers * rows * Hkv * max_seq, D], 64 x 64 boxes
   // workspace pieces
   int* status;
   void *xn, *qkv, *attn, *act;
@@ -124,7 +125,7 @@ int model_gemm(Model* m, int epi, const CUtensorMap& map, const void* w, const v
   const EesdModelDesc& d = m->d;
   if (d.dtype == EESD_BF16) {
     const int rc = tc_gemm_launch(epi, map, x, n_tok, n_out, k, up_offset, res, n_out, y, n_out, m->keys,
-                                  m->status, s);
+                                  m->status, s, d.weights_packed);
     m->launches += 1;
     return rc ? fail(rc, "tcgen05 gemm launch failed (n_tok=%d n_out=%d k=%d epi=%d)", n_tok, n_out, k, epi) : 0;
   }
@@ -180,6 +181,8 @@ int eesd_model_create(const EesdModelDesc* d, void** out) {
   if (d->max_seq % 64 || d->max_batch <= 0 || d->max_tokens <= 0) return fail(EESD_ERR_ARG, "bad cache/batch sizes");
   if (d->dtype == EESD_BF16 && (d->dim % 64 || d->intermediate % 64 || (d->n_heads * d->head_dim) % 64))
     return fail(EESD_ERR_ARG, "bf16 path needs dim, intermediate and Hq*D multiples of 64");
+  if (d->weights_packed && (d->dtype != EESD_BF16 || d->intermediate % 128))
+    return fail(EESD_ERR_ARG, "packed weights need bf16 and intermediate %% 128 == 0");
   const Layout L = layout_for(*d);
   if (!d->workspace || d->workspace_bytes < L.total)
     return fail(EESD_ERR_ARG, "workspace too small: %zu < %zu", d->workspace_bytes, L.total);
@@ -213,19 +216,32 @@ int eesd_model_create(const EesdModelDesc* d, void** out) {
     m->map_o.resize(d->n_layers);
     m->map_13.resize(d->n_layers);
     m->map_2.resize(d->n_layers);
+    auto enc = [&](CUtensorMap* map, const void* w, int rows, int k) {
+      return d->weights_packed ? encode_packed_map(map, w, rows, k) : encode_kmajor_map(map, w, rows, k, 128);
+    };
     for (int i = 0; i < d->n_layers; ++i) {
-      int rc = encode_kmajor_map(&m->map_qkv[i], m->wqkv[i], m->qkv_dim, d->dim, 128);
-      if (!rc) rc = encode_kmajor_map(&m->map_o[i], m->wo[i], d->dim, m->q_dim, 128);
-      if (!rc) rc = encode_kmajor_map(&m->map_13[i], m->w13[i], 2 * d->intermediate, d->dim, 128);
-      if (!rc) rc = encode_kmajor_map(&m->map_2[i], m->w2[i], d->dim, d->intermediate, 128);
+      int rc = enc(&m->map_qkv[i], m->wqkv[i], m->qkv_dim, d->dim);
+      if (!rc) rc = enc(&m->map_o[i], m->wo[i], d->dim, m->q_dim);
+      if (!rc) rc = enc(&m->map_13[i], m->w13[i], 2 * d->intermediate, d->dim);
+      if (!rc) rc = enc(&m->map_2[i], m->w2[i], d->dim, d->intermediate);
       if (rc) {
         delete m;
         return fail(rc, "tensor map encode failed for layer %d (16-byte aligned weights required)", i);
       }
     }
-    if (encode_kmajor_map(&m->map_head, d->lm_head, d->vocab, d->dim, 128)) {
+    if (enc(&m->map_head, d->lm_head, d->vocab, d->dim)) {
       delete m;
       return fail(EESD_ERR_CUDA, "tensor map encode failed for the LM head");
+    }
+    const long long cache_rows = (long long)d->n_layers * d->max_batch * d->n_kv_heads * d->max_seq;
+    if (cache_rows >= (1LL << 31)) {
+      delete m;
+      return fail(EESD_ERR_ARG, "KV cache too large for 32-bit TMA row coordinates");
+    }
+    if (encode_kmajor_map(&m->map_kc, d->k_cache, (int)cache_rows, d->head_dim, 64) ||
+        encode_kmajor_map(&m->map_vc, d->v_cache, (int)cache_rows, d->head_dim, 64)) {
+      delete m;
+      return fail(EESD_ERR_CUDA, "tensor map encode failed for the KV cache");
     }
   }
   // the status word starts at zero
@@ -280,7 +296,8 @@ int eesd_forward_layers(void* h, void* x, const EesdBatch* b, int start, int end
     m->launches++;
     if (rc) return fail(rc, "rope/kv launch");
     prof_begin(m, s, EESD_PROF_ATTN, &pe, N);
-    rc = launch_attention(d.dtype, g, m->qkv, kc, vc, m->attn, b->blk, b->items, b->n_items, b->max_ctx, m->status, s);
+    rc = launch_attention(d.dtype, g, m->qkv, d.k_cache, d.v_cache, m->attn, b->blk, b->items, b->n_items, b->max_ctx,
+                          m->status, s, &m->map_kc, &m->map_vc, i);
     prof_end(m, s, &pe);
     m->launches++;
     if (rc) return fail(rc, "attention launch");
@@ -493,6 +510,15 @@ int eesd_gemm(int dtype, int epilogue, const void* x, const void* w, const void*
   return rc ? fail(rc, "fp32 gemm launch") : EESD_OK;
 }
 
+size_t eesd_packed_weight_bytes(int rows, int k) {
+  return (rows > 0 && k > 0 && k % 64 == 0) ? packed_weight_bytes(rows, k) : 0;
+}
+
+int eesd_pack_weight(const void* w, int rows, int k, void* out, void* stream) {
+  const int rc = pack_weight(w, rows, k, out, static_cast<cudaStream_t>(stream));
+  return rc ? fail(rc, "pack_weight: rows %d k %d (k %% 64 == 0, 16-byte aligned pointers)", rows, k) : EESD_OK;
+}
+
 int eesd_status_read(const int32_t* status, int* bits_out, void* stream) {
   if (!status) return fail(EESD_ERR_ARG, "null status");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -508,6 +534,16 @@ int eesd_set_option(int option, int value) {
   if (option == 1) {   // tcgen05 MMA N: 0 = whole token tile, else a fixed multiple of 16
     if (value < 0 || value > 256 || value % 16) return fail(EESD_ERR_ARG, "mma n %d", value);
     tc_set_mma_n(value);
+    return EESD_OK;
+  }
+  if (option == 2) {   // tcgen05 split-K count: 0 = from the weight shape (changes summation order)
+    if (value < 0 || value > 8) return fail(EESD_ERR_ARG, "splits %d", value);
+    tc_set_splits(value);
+    return EESD_OK;
+  }
+  if (option == 3) {   // tcgen05 pipeline stages: 0 = as many as fit
+    if (value < 0 || value > 8 || value == 1) return fail(EESD_ERR_ARG, "stages %d", value);
+    tc_set_stages(value);
     return EESD_OK;
   }
   return fail(EESD_ERR_ARG, "unknown option %d", option);

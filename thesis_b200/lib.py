@@ -13,7 +13,7 @@ LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libeesd.so"
 OK, ERR_ARG, ERR_CUDA, ERR_DEVICE = 0, 1, 2, 3
 BF16, F32 = 0, 1
 EPI_STORE, EPI_RESIDUAL, EPI_SWIGLU = 0, 1, 2
-OPT_MMA_N = 1
+OPT_MMA_N, OPT_SPLITS, OPT_STAGES = 1, 2, 3
 PROF_KINDS = 9
 PROF_NAMES = ["norm", "gemm_qkv", "rope_kv", "attn", "gemm_o", "gemm_w13", "gemm_w2", "head", "misc"]
 
@@ -25,7 +25,7 @@ class ModelDesc(C.Structure):
     _fields_ = [
         ("dtype", i32), ("n_layers", i32), ("dim", i32), ("n_heads", i32), ("n_kv_heads", i32), ("head_dim", i32),
         ("intermediate", i32), ("vocab", i32), ("norm_eps", f32), ("max_batch", i32), ("max_seq", i32),
-        ("max_tokens", i32), ("wqkv", C.POINTER(vp)), ("wo", C.POINTER(vp)), ("w13", C.POINTER(vp)),
+        ("max_tokens", i32), ("weights_packed", i32), ("wqkv", C.POINTER(vp)), ("wo", C.POINTER(vp)), ("w13", C.POINTER(vp)),
         ("w2", C.POINTER(vp)), ("attn_norm", C.POINTER(vp)), ("ffn_norm", C.POINTER(vp)), ("final_norm", vp),
         ("lm_head", vp), ("embed", vp), ("rope_cos", vp), ("rope_sin", vp), ("k_cache", vp), ("v_cache", vp),
         ("workspace", vp), ("workspace_bytes", sz),
@@ -42,6 +42,8 @@ SIGNATURES = {
     "eesd_version": (C.c_int, []),
     "eesd_last_error": (C.c_char_p, []),
     "eesd_attn_item_tokens": (C.c_int, [C.c_int, C.c_int]),
+    "eesd_packed_weight_bytes": (sz, [C.c_int, C.c_int]),
+    "eesd_pack_weight": (C.c_int, [vp, C.c_int, C.c_int, vp, vp]),
     "eesd_model_workspace_bytes": (sz, [C.POINTER(ModelDesc)]),
     "eesd_model_create": (C.c_int, [C.POINTER(ModelDesc), C.POINTER(vp)]),
     "eesd_model_destroy": (C.c_int, [vp]),
@@ -94,7 +96,7 @@ def check(rc: int, what: str = "") -> None:
 
 
 # entry points that launch exactly one kernel (counted for the bench's launch total)
-KERNEL_CALLS = {"eesd_copy_rows", "eesd_gather_ids", "eesd_scatter_ids", "eesd_greedy_accept", "eesd_rmsnorm",
+KERNEL_CALLS = {"eesd_pack_weight", "eesd_copy_rows", "eesd_gather_ids", "eesd_scatter_ids", "eesd_greedy_accept", "eesd_rmsnorm",
                 "eesd_gemm"}
 direct_launches = 0
 

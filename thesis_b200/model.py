@@ -74,6 +74,7 @@ class ModelWeights:
             self.t[k] = v
         if cfg.tie_word_embeddings or "lm_head" not in self.t:
             self.t["lm_head"] = self.t["embed"]
+        self._packed = {}
         for i in range(cfg.n_layers):
             for name in ("wqkv", "wo", "w13", "w2", "attn_norm", "ffn_norm"):
                 if f"l{i}.{name}" not in self.t:
@@ -82,6 +83,23 @@ class ModelWeights:
     @property
     def n_layers(self) -> int:
         return self.cfg.n_layers
+
+    def packs_gemm_weights(self) -> bool:
+        """bf16 GEMM weights are streamed from a tile-packed copy (contiguous 16 KB tiles)."""
+        return self.dtype == torch.bfloat16 and self.cfg.intermediate_size % 128 == 0
+
+    def packed(self, key: str) -> torch.Tensor:
+        """Tile-packed copy of a GEMM weight (``eesd_pack_weight``), built once and cached."""
+        if key not in self._packed:
+            w = self.t[key]
+            rows, k = w.shape
+            n = lib.load().eesd_packed_weight_bytes(rows, k)
+            if n == 0:
+                raise ValueError(f"{key}: cannot pack a [{rows}, {k}] weight (k must be a multiple of 64)")
+            out = torch.empty(n // 2, dtype=torch.bfloat16, device=self.device)
+            lib.call("eesd_pack_weight", w.data_ptr(), rows, k, out.data_ptr(), lib.stream_ptr())
+            self._packed[key] = out
+        return self._packed[key]
 
     def layer_bytes(self) -> int:
         return sum(self.t[f"l0.{n}"].numel() for n in ("wqkv", "wo", "w13", "w2", "attn_norm", "ffn_norm")) * \
@@ -172,10 +190,16 @@ class DeviceModel:
         self.k_cache = torch.zeros(shape, dtype=self.dtype, device=self.device)
         self.v_cache = torch.zeros(shape, dtype=self.dtype, device=self.device)
         t = weights.t
+        packed = weights.packs_gemm_weights()
         self._ptr_arrays = {}
 
+        def gemm_w(key):
+            return (weights.packed(key) if packed else t[key]).data_ptr()
+
         def arr(name):
-            a = (C.c_void_p * cfg.n_layers)(*[t[f"l{i}.{name}"].data_ptr() for i in range(cfg.n_layers)])
+            ptrs = [gemm_w(f"l{i}.{name}") if name in ("wqkv", "wo", "w13", "w2") else t[f"l{i}.{name}"].data_ptr()
+                    for i in range(cfg.n_layers)]
+            a = (C.c_void_p * cfg.n_layers)(*ptrs)
             self._ptr_arrays[name] = a
             return C.cast(a, C.POINTER(C.c_void_p))
 
@@ -185,9 +209,10 @@ class DeviceModel:
         d.head_dim, d.intermediate, d.vocab = cfg.head_dim, cfg.intermediate_size, cfg.vocab_size
         d.norm_eps = cfg.norm_eps
         d.max_batch, d.max_seq, d.max_tokens = self.max_batch, self.max_seq, self.max_tokens
+        d.weights_packed = int(packed)
         d.wqkv, d.wo, d.w13, d.w2 = arr("wqkv"), arr("wo"), arr("w13"), arr("w2")
         d.attn_norm, d.ffn_norm = arr("attn_norm"), arr("ffn_norm")
-        d.final_norm, d.lm_head, d.embed = t["norm"].data_ptr(), t["lm_head"].data_ptr(), t["embed"].data_ptr()
+        d.final_norm, d.lm_head, d.embed = t["norm"].data_ptr(), gemm_w("lm_head"), t["embed"].data_ptr()
         d.rope_cos, d.rope_sin = self.rope_cos.data_ptr(), self.rope_sin.data_ptr()
         d.k_cache, d.v_cache = self.k_cache.data_ptr(), self.v_cache.data_ptr()
         ws = L.eesd_model_workspace_bytes(C.byref(d))
