@@ -42,8 +42,6 @@ constexpr int kThreads = 320;
 constexpr int kEpiThreads = 256;           // warps 2..9
 constexpr uint32_t kATileBytes = kBM * kBK * 2;
 constexpr size_t kSmemBudget = 224 * 1024;
-constexpr int kRedCols = 64;               // split-K reduction chunk (token columns)
-constexpr int kRedGroups = kRedCols / 4;   // float4 groups per row; group g of row r sits at g ^ (r & 15)
 constexpr int kMaxSplits = 8;              // portable cluster size
 
 struct alignas(8) TcParams {
@@ -58,6 +56,7 @@ struct alignas(8) TcParams {
   int up_offset;    // SwiGLU: row of the first 'up' weight
   int tmem_cols;
   int a_packed;     // 1: weight in tile-packed layout (3-D map over 16 KB tiles), 0: row-major 2-D map
+  int red_cols;     // split-K: token columns reduced per pass (multiple of 64)
   const bf16* residual;
   int ld_res;
   bf16* y;
@@ -80,12 +79,12 @@ __device__ __forceinline__ uint32_t dsmem_addr(uint32_t local, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
   return r;
 }
-// Plain (non-volatile) 16-byte DSMEM load: ordering against the writers comes from the cluster
-// barrier, so several loads can be in flight at once.
-__device__ __forceinline__ float4 dsmem_ld4(uint32_t addr) {
-  float4 v;
-  asm("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
-  return v;
+// 16-byte store into (possibly another CTA's) shared memory of the cluster; visibility to the
+// reader comes from the cluster barrier (release / acquire).
+__device__ __forceinline__ void dsmem_st4(uint32_t addr, float4 v) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z),
+               "f"(v.w)
+               : "memory");
 }
 
 // silu(x) = x / (1 + exp(-x)) with the fast exponential and division (results are rounded to bf16)
@@ -300,54 +299,79 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // ---------------- split-K through distributed shared memory (all threads take every barrier)
+    // ---------------- split-K through distributed shared memory (all threads take every barrier).
+    // Passes of red_cols token columns; inside a pass, CTA r of the cluster owns the column slice
+    // [r * slice, (r + 1) * slice).  Every CTA pushes each owner its fp32 partial of that slice
+    // (st.shared::cluster into the owner's idle stage memory, laid out [split][part][slice/4][128]
+    // float4, so a warp's 32 rows are 512 contiguous bytes for both the pushes and the sums),
+    // then after one cluster barrier every owner sums the splits in order from local shared memory
+    // with all 320 threads and runs the epilogue.
     constexpr int kParts = (EPI == EESD_EPI_SWIGLU) ? 2 : 1;
-    float4* red = reinterpret_cast<float4*>(smem);                // [kParts][128][kRedGroups] (swizzled)
+    float4* red = reinterpret_cast<float4*>(smem);
     const uint32_t red_u32 = smem_u32(red);
     const uint32_t rank = cluster_rank();
-    const int sw = row_local & 15;
-    for (int c0 = 0; c0 < p.bn; c0 += kRedCols) {
-      const int cw = min(kRedCols, p.bn - c0);
+    // every CTA of the cluster must be past its main loop (its stage memory idle) before any CTA
+    // pushes partial sums into it
+    cluster_sync();
+    for (int c0 = 0; c0 < p.bn; c0 += p.red_cols) {
+      const int cw = min(p.red_cols, p.bn - c0);
+      const int slice = (((cw + p.splits - 1) / p.splits) + 15) / 16 * 16;      // columns per owner
+      const int sg = slice / 4;                                                // float4 groups per row
       if (epi_warp && ok) {
         for (int cc = half * 16; cc < cw; cc += 32) {
+          const int owner = cc / slice, gbase = (cc - owner * slice) / 4;
+          const uint32_t dst_base = dsmem_addr(red_u32, (uint32_t)owner);
 #pragma unroll
           for (int part = 0; part < kParts; ++part) {
             float v[16];
             tmem_ld16(lane_base + part * p.bn + c0 + cc, v);
-            float4* dst = red + (part * 128 + row_local) * kRedGroups;
+            const int gpart = ((int)rank * kParts + part) * sg;
 #pragma unroll
             for (int j = 0; j < 4; ++j)
-              dst[((cc >> 2) + j) ^ sw] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+              dsmem_st4(dst_base + (uint32_t)((gpart + gbase + j) * 128 + row_local) * 16u,
+                        make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
           }
         }
       }
       cluster_sync();
-      if (epi_warp && ok) {
-        // this CTA reduces column groups [glo, ghi) of the chunk (halves alternate groups),
-        // summing the splits in order
-        const int ng = cw >> 2;
-        const int per = (ng + p.splits - 1) / p.splits;
-        const int glo = rank * per, ghi = min(ng, glo + per);
-        for (int gi = glo + half; gi < ghi; gi += 2) {
-          float g[4] = {0.f, 0.f, 0.f, 0.f}, u[4] = {0.f, 0.f, 0.f, 0.f};
-          const uint32_t off0 = (uint32_t)((row_local * kRedGroups + (gi ^ sw)) * 16);
-          const uint32_t off1 = (uint32_t)(((128 + row_local) * kRedGroups + (gi ^ sw)) * 16);
-          for (int s = 0; s < p.splits; ++s) {
-            const uint32_t base = dsmem_addr(red_u32, (uint32_t)s);
-            const float4 a = dsmem_ld4(base + off0);
-            g[0] += a.x;
-            g[1] += a.y;
-            g[2] += a.z;
-            g[3] += a.w;
-            if (kParts == 2) {
-              const float4 b = dsmem_ld4(base + off1);
-              u[0] += b.x;
-              u[1] += b.y;
-              u[2] += b.z;
-              u[3] += b.w;
+      {
+        const int cbase = (int)rank * slice;                                   // first column owned
+        const int my_groups = max(0, min(slice, cw - cbase)) / 4;
+        const int items = 128 * my_groups;
+        for (int i0 = threadIdx.x; i0 < items; i0 += 4 * kThreads) {
+          float g[4][4], u[4][4];
+          int rl[4], gi[4];
+#pragma unroll
+          for (int b = 0; b < 4; ++b) {
+            const int i = i0 + b * kThreads;
+            rl[b] = i % 128;
+            gi[b] = i / 128;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) g[b][e] = u[b][e] = 0.f;
+            if (i < items) {
+              for (int sp = 0; sp < p.splits; ++sp) {
+                const float4 a = red[((sp * kParts) * sg + gi[b]) * 128 + rl[b]];
+                g[b][0] += a.x;
+                g[b][1] += a.y;
+                g[b][2] += a.z;
+                g[b][3] += a.w;
+                if (kParts == 2) {
+                  const float4 c = red[((sp * kParts + 1) * sg + gi[b]) * 128 + rl[b]];
+                  u[b][0] += c.x;
+                  u[b][1] += c.y;
+                  u[b][2] += c.z;
+                  u[b][3] += c.w;
+                }
+              }
             }
           }
-          if (row_ok) epilogue_cols<EPI, 4>(p, n0 + c0 + 4 * gi, row, g, u);
+#pragma unroll
+          for (int b = 0; b < 4; ++b) {
+            const int i = i0 + b * kThreads;
+            const int row_b = m0 + rl[b];
+            if (i < items && ok && row_b < p.n_out)
+              epilogue_cols<EPI, 4>(p, n0 + c0 + cbase + 4 * gi[b], row_b, g[b], u[b]);
+          }
         }
       }
       cluster_sync();
@@ -521,6 +545,13 @@ TcPlan tc_plan(int n_tok, int n_out, int k, int epi) {
   pl.stages = (int)std::min<size_t>(8, kSmemBudget / stage);
   if (g_stages_option >= 2 && (size_t)g_stages_option * stage <= kSmemBudget) pl.stages = g_stages_option;
   pl.smem = (size_t)pl.stages * stage + 1024 + 256;
+  // split-K reduction pass width: the whole (64-rounded) tile if it fits the stage memory
+  auto red_need = [&](int cols) {
+    const int slice = ((cols + pl.splits - 1) / pl.splits + 15) / 16 * 16;
+    return (size_t)na * 128 * (size_t)slice * pl.splits * 4;
+  };
+  pl.red_cols = (pl.bn + 63) / 64 * 64;
+  while (pl.red_cols > 64 && red_need(pl.red_cols) > (size_t)pl.stages * stage) pl.red_cols -= 64;
   pl.tmem_cols = next_pow2(na * pl.bn);
   return pl;
 }
@@ -533,10 +564,12 @@ int tc_gemm_launch(int epi, const CUtensorMap& map_w, const void* x, int n_tok, 
   const TcPlan pl = tc_plan(n_tok, n_out, k, epi);
   if (pl.stages < 2) return EESD_ERR_ARG;
   // the split-K reduction buffer lives in the (then idle) stage memory
-  const size_t red_bytes = (size_t)(epi == EESD_EPI_SWIGLU ? 2 : 1) * 128 * kRedCols * 4;
-  if (pl.splits > 1 && red_bytes > (size_t)pl.stages * ((epi == EESD_EPI_SWIGLU ? 2 : 1) * kATileBytes +
-                                                        (size_t)pl.bn * kBK * 2))
-    return EESD_ERR_ARG;
+  {
+    const int na = epi == EESD_EPI_SWIGLU ? 2 : 1;
+    const int slice = ((pl.red_cols + pl.splits - 1) / pl.splits + 15) / 16 * 16;
+    const size_t red_bytes = (size_t)na * 128 * slice * pl.splits * 4;
+    if (pl.splits > 1 && red_bytes > (size_t)pl.stages * (na * kATileBytes + (size_t)pl.bn * kBK * 2)) return EESD_ERR_ARG;
+  }
   CUtensorMap map_x;
   int rc = encode_kmajor_map(&map_x, x, n_tok, k, pl.b_boxes == 2 ? pl.bn / 2 : pl.bn);
   if (rc) return rc;
@@ -554,6 +587,7 @@ int tc_gemm_launch(int epi, const CUtensorMap& map_w, const void* x, int n_tok, 
   p.up_offset = up_offset;
   p.tmem_cols = pl.tmem_cols;
   p.a_packed = a_packed;
+  p.red_cols = pl.red_cols;
   p.residual = static_cast<const bf16*>(residual);
   p.ld_res = ld_res;
   p.y = static_cast<bf16*>(y);

@@ -14,7 +14,7 @@ typedef CUresult (*PFN_encodeTiled_t)(CUtensorMap*, CUtensorMapDataType, cuuint3
                                       CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 struct TcPlan {
-  int tok_tiles, out_tiles, bn, b_boxes, mma_n, kb_total, kb_per, splits, stages, tmem_cols;
+  int tok_tiles, out_tiles, bn, b_boxes, mma_n, kb_total, kb_per, splits, stages, tmem_cols, red_cols;
   size_t smem;
 };
 
