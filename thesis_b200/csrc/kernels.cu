@@ -10,6 +10,13 @@ namespace eesd {
 
 namespace {
 
+// 2^x with the hardware approximation (ex2.approx; 2^-inf = 0)
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -361,6 +368,7 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(const __grid_constant__ 
     for (int n = 0; n < ND; ++n) o[rg][n][0] = o[rg][n][1] = o[rg][n][2] = o[rg][n][3] = 0.f;
   }
   const int kw = warp * 16;                             // this warp's keys inside every tile
+  const float scale_l2 = g.scale * 1.4426950408889634f;  // softmax scale times log2(e)
 
   for (int tile = 0; tile < n_tiles; ++tile) {
     if (threadIdx.x == 0 && tile + NS - 1 < n_tiles) issue(tile + NS - 1);
@@ -385,15 +393,22 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(const __grid_constant__ 
           mma_bf16(s[0], a0, a1, a2, a3, b0, b1);
           mma_bf16(s[1], a0, a1, a2, a3, b2, b3);
         }
+        // scores in the log2 domain (scale * log2 e folded in); only tiles reaching past the
+        // item's first query position need the causal mask
         const int kbase = tile * KT + kw + 2 * tq;
+        const bool need_mask = tile * KT + kw + 15 > pos0 + t0;
         float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
         for (int n = 0; n < 2; ++n) {
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
-            const int key = kbase + n * 8 + e;
-            s[n][e] = key <= qpos[rg][0] ? s[n][e] * g.scale : -INFINITY;
-            s[n][2 + e] = key <= qpos[rg][1] ? s[n][2 + e] * g.scale : -INFINITY;
+            s[n][e] *= scale_l2;
+            s[n][2 + e] *= scale_l2;
+            if (need_mask) {
+              const int key = kbase + n * 8 + e;
+              if (key > qpos[rg][0]) s[n][e] = -INFINITY;
+              if (key > qpos[rg][1]) s[n][2 + e] = -INFINITY;
+            }
             mx0 = fmaxf(mx0, s[n][e]);
             mx1 = fmaxf(mx1, s[n][2 + e]);
           }
@@ -403,8 +418,10 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(const __grid_constant__ 
         mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
         mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
         const float mn0 = fmaxf(m[rg][0], mx0), mn1 = fmaxf(m[rg][1], mx1);
+        // the running output needs rescaling only when some row's maximum moved
+        const bool moved = !__all_sync(0xffffffffu, mn0 == m[rg][0] && mn1 == m[rg][1]);
         const float ms0 = mn0 == -INFINITY ? 0.f : mn0, ms1 = mn1 == -INFINITY ? 0.f : mn1;
-        const float c0 = __expf(m[rg][0] - ms0), c1 = __expf(m[rg][1] - ms1);
+        const float c0 = fast_exp2(m[rg][0] - ms0), c1 = fast_exp2(m[rg][1] - ms1);
         m[rg][0] = mn0;
         m[rg][1] = mn1;
         float ps0 = 0.f, ps1 = 0.f;
@@ -412,8 +429,8 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(const __grid_constant__ 
         for (int n = 0; n < 2; ++n) {
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
-            s[n][e] = __expf(s[n][e] - ms0);
-            s[n][2 + e] = __expf(s[n][2 + e] - ms1);
+            s[n][e] = fast_exp2(s[n][e] - ms0);
+            s[n][2 + e] = fast_exp2(s[n][2 + e] - ms1);
             ps0 += s[n][e];
             ps1 += s[n][2 + e];
           }
@@ -422,16 +439,17 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(const __grid_constant__ 
         l[rg][1] = l[rg][1] * c1 + ps1;
         const uint32_t p0 = pack_bf16(s[0][0], s[0][1]), p1 = pack_bf16(s[0][2], s[0][3]);
         const uint32_t p2 = pack_bf16(s[1][0], s[1][1]), p3 = pack_bf16(s[1][2], s[1][3]);
+        if (moved) {
+#pragma unroll
+          for (int n = 0; n < ND; ++n) {
+            o[rg][n][0] *= c0;
+            o[rg][n][1] *= c0;
+            o[rg][n][2] *= c1;
+            o[rg][n][3] *= c1;
+          }
+        }
 #pragma unroll
         for (int n2 = 0; n2 < ND; n2 += 2) {
-          o[rg][n2][0] *= c0;
-          o[rg][n2][1] *= c0;
-          o[rg][n2][2] *= c1;
-          o[rg][n2][3] *= c1;
-          o[rg][n2 + 1][0] *= c0;
-          o[rg][n2 + 1][1] *= c0;
-          o[rg][n2 + 1][2] *= c1;
-          o[rg][n2 + 1][3] *= c1;
           const int key = kw + (lane & 7) + ((lane >> 3) & 1) * 8;
           const int dim = n2 * 8 + (lane >> 4) * 8;
           const uint32_t chunk = (uint32_t)((dim & 63) >> 3) ^ (uint32_t)(key & 7);
@@ -483,7 +501,7 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(const __grid_constant__ 
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
       const float mw = Ms[w * 32 + r];
-      const float f = mw == -INFINITY ? 0.f : __expf(mw - mx);
+      const float f = mw == -INFINITY ? 0.f : fast_exp2(mw - mx);
       const float2 ov = *reinterpret_cast<const float2*>(&Ow[(w * 32 + r) * OLD + d]);
       lsum += Lw[w * 32 + r] * f;
       a += ov.x * f;
