@@ -109,8 +109,9 @@ __device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t a_desc, uin
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+  // no memory clobber: the MMA reads shared memory asynchronously, and its ordering against the
+  // barrier waits, fences and commits (all volatile asm) is kept by volatility alone
 }
 // arrive on an mbarrier once every previously issued tcgen05.mma of this thread completed
 __device__ __forceinline__ void tc_commit(uint32_t bar) {
@@ -197,6 +198,7 @@ inline cudaError_t launch_cluster_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 
 
 // ------------------------------------------------------------------ thread-block clusters
 __device__ __forceinline__ void cluster_sync() {
+  __syncwarp();   // .aligned: the whole warp executes the barrier together
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 __device__ __forceinline__ uint32_t cluster_rank() {

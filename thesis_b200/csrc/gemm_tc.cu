@@ -65,7 +65,11 @@ struct alignas(8) TcParams {
   int* status;
 };
 
-__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+// named barrier of the 256 epilogue threads (bar.sync counts whole warps: converge first)
+__device__ __forceinline__ void epi_bar() {
+  __syncwarp();
+  asm volatile("bar.sync 1, 256;" ::: "memory");
+}
 // 16-byte store into (possibly another CTA's) shared memory of the cluster; visibility to the
 // reader comes from the cluster barrier (release / acquire).
 __device__ __forceinline__ void dsmem_st4(uint32_t addr, float4 v) {
@@ -179,46 +183,60 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       pdl_wait();
       for (int i = 0; i < pre; ++i) load_b(i, smem_u32(smem + (size_t)i * stage_bytes), smem_u32(&full[i]));
+      const int stages = p.stages;
+      const uint32_t smem0 = smem_u32(smem), full0 = smem_u32(full), empty0 = smem_u32(empty);
+      int s = pre % stages, ph = (pre / stages) & 1;   // ring slot of k-block i and its fill parity
       for (int i = pre; i < nkb; ++i) {
-        const int s = i % p.stages, r = i / p.stages;
-        if (!mbar_wait(smem_u32(&empty[s]), (r - 1) & 1, abort_flag)) {
+        // slot s was last filled for k-block i - stages: wait for the MMAs that read it
+        if (!mbar_wait(empty0 + 8u * s, ph ^ 1, abort_flag)) {
           set_status(p.status, kStatusTimeoutProducer);
           *abort_flag = 1;
           break;
         }
-        const uint32_t fb = smem_u32(&full[s]);
+        const uint32_t fb = full0 + 8u * s;
         mbar_arrive_expect_tx(fb, stage_bytes);
-        const uint32_t st = smem_u32(smem + (size_t)s * stage_bytes);
+        const uint32_t st = smem0 + (uint32_t)s * stage_bytes;
         load_a(i, st, fb);
         load_b(i, st, fb);
+        if (++s == stages) { s = 0; ph ^= 1; }
       }
     }
     __syncwarp();
   } else if (warp == 1) {
     if (lane == 0) {
+      // This single-thread loop is on the critical path (one tcgen05.mma per 4 KB of weights at
+      // small token counts): loop-invariant values live in registers, descriptors are built once
+      // per stage and stepped by adding to their 14-bit start-address field (bytes / 16).
       const uint32_t idesc = idesc_bf16_f32(kBM, p.mma_n);
+      const int stages = p.stages, bn = p.bn, mma_n = p.mma_n;
+      const uint32_t full0 = smem_u32(full), empty0 = smem_u32(empty);
+      const uint64_t desc_hi = sw128_kmajor_desc(0);
+      const uint32_t a_lo0 = smem_u32(smem) >> 4, stage_lo = stage_bytes >> 4;
+      const uint32_t sub_lo = (uint32_t)mma_n * 8u;   // mma_n rows of 128 B, in 16-byte units
       bool ok = true;
+      int s = 0, ph = 0;
       for (int i = 0; i < nkb; ++i) {
-        const int s = i % p.stages, r = i / p.stages;
-        if (!mbar_wait(smem_u32(&full[s]), r & 1, abort_flag)) {
+        if (!mbar_wait(full0 + 8u * s, ph, abort_flag)) {
           set_status(p.status, kStatusTimeoutMma);
           *abort_flag = 1;
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t a0 = smem_u32(smem + (size_t)s * stage_bytes);
-        const uint32_t b0 = a0 + kNA * kATileBytes;
+        const uint64_t da = desc_hi | (uint64_t)(a_lo0 + (uint32_t)s * stage_lo);
+        const uint64_t db = da + (uint64_t)(kNA * (kATileBytes >> 4));
 #pragma unroll
         for (int kk = 0; kk < kBK / 16; ++kk) {
           const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
-          for (int nb = 0; nb < p.bn; nb += p.mma_n) {
-            const uint64_t bd = sw128_kmajor_desc(b0 + (uint32_t)nb * 128u + kk * 32u);
-            tc_mma_f16(tmem_base + nb, sw128_kmajor_desc(a0 + kk * 32u), bd, idesc, acc);
-            if (kNA == 2) tc_mma_f16(tmem_base + p.bn + nb, sw128_kmajor_desc(a0 + kATileBytes + kk * 32u), bd, idesc, acc);
+          const uint64_t a_k = da + 2u * kk;            // +32 bytes along K
+          uint64_t b_k = db + 2u * kk;
+          for (int nb = 0; nb < bn; nb += mma_n, b_k += sub_lo) {
+            tc_mma_f16(tmem_base + nb, a_k, b_k, idesc, acc);
+            if (kNA == 2) tc_mma_f16(tmem_base + bn + nb, a_k + (kATileBytes >> 4), b_k, idesc, acc);
           }
         }
-        tc_commit(smem_u32(&empty[s]));
+        tc_commit(empty0 + 8u * s);
+        if (++s == stages) { s = 0; ph ^= 1; }
       }
       if (ok) tc_commit(smem_u32(accb));
     }
@@ -365,6 +383,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   tc_fence_before();
+  __syncwarp();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
