@@ -49,9 +49,16 @@ def test_workspace_sizes(L):
     d.intermediate, d.vocab, d.max_batch, d.max_seq, d.max_tokens = 14336, 128256, 64, 1088, 2048
     ws = L.eesd_model_workspace_bytes(C.byref(d))
     acts = 2048 * (4096 + 6144 + 4096 + 14336) * 2
-    assert acts < ws < acts + (1 << 22)            # split-K partials never touch global memory
-    assert L.eesd_gemm_workspace_bytes(64, 6144, 4096, lib.EPI_STORE) == 256      # the status word
-    assert L.eesd_gemm_workspace_bytes(64, 512, 4096, lib.EPI_SWIGLU) == 256 + 64 * 1024 * 4
+    # split-K partial tiles: output tiles x token tiles x splits x 128 rows x columns x fp32; the
+    # largest is O / W2 at 2048 tokens (32 row tiles, 6 token tiles of 352, 4 splits)
+    partials = 32 * 6 * 4 * 128 * 352 * 4
+    assert acts + partials < ws < acts + partials + (1 << 22)
+    # status word + QKV partials (48 row tiles, 2 splits, 64 tokens)
+    assert L.eesd_gemm_workspace_bytes(64, 6144, 4096, lib.EPI_STORE) == 256 + 48 * 2 * 128 * 64 * 4
+    # status word + fp32-path scratch + SwiGLU partials (4 row tiles, 4 splits, gate + up columns)
+    assert L.eesd_gemm_workspace_bytes(64, 512, 4096, lib.EPI_SWIGLU) == 256 + 64 * 1024 * 4 + 4 * 4 * 128 * 128 * 4
+    # the LM-head-sized weight is never split
+    assert L.eesd_gemm_workspace_bytes(64, 128256, 4096, lib.EPI_STORE) == 256
     assert L.eesd_gemm_workspace_bytes(0, 6144, 4096, lib.EPI_STORE) == 0
 
 

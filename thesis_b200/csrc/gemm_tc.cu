@@ -56,12 +56,13 @@ struct alignas(8) TcParams {
   int up_offset;    // SwiGLU: row of the first 'up' weight
   int tmem_cols;
   int a_packed;     // 1: weight in tile-packed layout (3-D map over 16 KB tiles), 0: row-major 2-D map
-  int red_cols;     // split-K: token columns reduced per pass (multiple of 64)
+  int acc_cols;     // TMEM columns of the accumulator (bn, or 2 bn for SwiGLU)
   const bf16* residual;
   int ld_res;
   bf16* y;
   int ld_y;
   unsigned long long* keys;  // argmax keys [n_tok]
+  float4* partials;          // split-K: [tile][split][acc_cols / 4][128] fp32 partial tiles
   int* status;
 };
 
@@ -70,14 +71,6 @@ __device__ __forceinline__ void epi_bar() {
   __syncwarp();
   asm volatile("bar.sync 1, 256;" ::: "memory");
 }
-// 16-byte store into (possibly another CTA's) shared memory of the cluster; visibility to the
-// reader comes from the cluster barrier (release / acquire).
-__device__ __forceinline__ void dsmem_st4(uint32_t addr, float4 v) {
-  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z),
-               "f"(v.w)
-               : "memory");
-}
-
 // silu(x) = x / (1 + exp(-x)) with the fast exponential and division (results are rounded to bf16)
 __device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
@@ -85,13 +78,18 @@ __device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + _
 // before any store (the residual may be the output buffer itself, so interleaving would serialise
 // every load behind the previous store).
 template <int EPI, int NC>
-__device__ __forceinline__ void epilogue_cols(const TcParams& p, int t0, int row, const float* g, const float* u) {
-  float r[NC];
+__device__ __forceinline__ void load_residual(const TcParams& p, int t0, int row, float* r) {
   if (EPI == EESD_EPI_RESIDUAL) {
 #pragma unroll
     for (int j = 0; j < NC; ++j)
       r[j] = (t0 + j < p.n_tok) ? __bfloat162float(p.residual[(size_t)(t0 + j) * p.ld_res + row]) : 0.f;
   }
+}
+
+// Epilogue with the residual values already loaded (r, RESIDUAL only)
+template <int EPI, int NC>
+__device__ __forceinline__ void epilogue_cols_r(const TcParams& p, int t0, int row, const float* g, const float* u,
+                                                const float* r) {
 #pragma unroll
   for (int j = 0; j < NC; ++j) {
     const int t = t0 + j;
@@ -108,6 +106,13 @@ __device__ __forceinline__ void epilogue_cols(const TcParams& p, int t0, int row
       p.y[o] = __float2bfloat16_rn(rnd<bf16>(silu_f(gb)) * ub);
     }
   }
+}
+
+template <int EPI, int NC>
+__device__ __forceinline__ void epilogue_cols(const TcParams& p, int t0, int row, const float* g, const float* u) {
+  float r[NC];
+  load_residual<EPI, NC>(p, t0, row, r);
+  epilogue_cols_r<EPI, NC>(p, t0, row, g, u, r);
 }
 
 template <int EPI>
@@ -304,82 +309,72 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // ---------------- split-K through distributed shared memory (all threads take every barrier).
-    // Passes of red_cols token columns; inside a pass, CTA r of the cluster owns the column slice
-    // [r * slice, (r + 1) * slice).  Every CTA pushes each owner its fp32 partial of that slice
-    // (st.shared::cluster into the owner's idle stage memory, laid out [split][part][slice/4][128]
-    // float4, so a warp's 32 rows are 512 contiguous bytes for both the pushes and the sums),
-    // then after one cluster barrier every owner sums the splits in order from local shared memory
-    // with all 320 threads and runs the epilogue.
-    constexpr int kParts = (EPI == EESD_EPI_SWIGLU) ? 2 : 1;
-    float4* red = reinterpret_cast<float4*>(smem);
-    const uint32_t red_u32 = smem_u32(red);
-    const uint32_t rank = cluster_rank();
-    // every CTA of the cluster must be past its main loop (its stage memory idle) before any CTA
-    // pushes partial sums into it
-    cluster_sync();
-    for (int c0 = 0; c0 < p.bn; c0 += p.red_cols) {
-      const int cw = min(p.red_cols, p.bn - c0);
-      const int slice = (((cw + p.splits - 1) / p.splits) + 15) / 16 * 16;      // columns per owner
-      const int sg = slice / 4;                                                // float4 groups per row
-      if (epi_warp && ok) {
-        for (int cc = half * 16; cc < cw; cc += 32) {
-          const int owner = cc / slice, gbase = (cc - owner * slice) / 4;
-          const uint32_t dst_base = dsmem_addr(red_u32, (uint32_t)owner);
+    // ---------------- split-K through L2.  CTA r of the cluster owns the token-column slice
+    // [r * slice, (r + 1) * slice) of the tile.  Every CTA stores its fp32 partial of the columns
+    // it does not own (laid out [column / 4][128 rows] float4: a warp's 32 rows are 512 contiguous
+    // bytes), one cluster barrier (release / acquire at cluster scope) publishes them, then every
+    // owner adds the splits in split order - its own straight from TMEM - and runs the epilogue.
+    // The cluster's CTAs are co-scheduled, so the barrier never waits on an unscheduled CTA.
+    const int S = p.splits;
+    const int rank = (int)cluster_rank();
+    const int slice = ((p.bn + S - 1) / S + 15) / 16 * 16;
+    const int own_lo = rank * slice, own_hi = min(p.bn, own_lo + slice);
+    const size_t part_f4 = (size_t)p.acc_cols * 32;   // float4s in one split's partial tile
+    float4* tile_parts = p.partials + (size_t)((out_tile * gridDim.x + tok_tile) * S) * part_f4;
+    if (epi_warp && ok) {
+      float4* mine = tile_parts + (size_t)rank * part_f4;
+      for (int c = half * 16; c < p.bn; c += 32) {
+        if (c >= own_lo && c < own_hi) continue;      // the owned slice stays in TMEM
 #pragma unroll
-          for (int part = 0; part < kParts; ++part) {
-            float v[16];
-            tmem_ld16(lane_base + part * p.bn + c0 + cc, v);
-            const int gpart = ((int)rank * kParts + part) * sg;
+        for (int part = 0; part < kNA; ++part) {
+          float v[16];
+          tmem_ld16(lane_base + part * p.bn + c, v);
+          const int g0 = (part * p.bn + c) / 4;
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-              dsmem_st4(dst_base + (uint32_t)((gpart + gbase + j) * 128 + row_local) * 16u,
-                        make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
-          }
+          for (int j = 0; j < 4; ++j)
+            mine[(size_t)(g0 + j) * 128 + row_local] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
         }
       }
-      cluster_sync();
-      {
-        const int cbase = (int)rank * slice;                                   // first column owned
-        const int my_groups = max(0, min(slice, cw - cbase)) / 4;
-        const int items = 128 * my_groups;
-        for (int i0 = threadIdx.x; i0 < items; i0 += 4 * kThreads) {
-          float g[4][4], u[4][4];
-          int rl[4], gi[4];
+    }
+    cluster_sync();
+    if (epi_warp && ok) {
+      for (int c = half * 16; c < p.bn; c += 32) {
+        if (c < own_lo || c >= own_hi) continue;
+        float g[16], u[16];
 #pragma unroll
-          for (int b = 0; b < 4; ++b) {
-            const int i = i0 + b * kThreads;
-            rl[b] = i % 128;
-            gi[b] = i / 128;
+        for (int j = 0; j < 16; ++j) g[j] = u[j] = 0.f;
+#pragma unroll 2
+        for (int sp = 0; sp < S; ++sp) {
+          float pg[16], pu[16];
+          if (sp == rank) {
+            tmem_ld16(lane_base + c, pg);
+            if (kNA == 2) tmem_ld16(lane_base + p.bn + c, pu);
+          } else {
+            const float4* src = tile_parts + (size_t)sp * part_f4;
 #pragma unroll
-            for (int e = 0; e < 4; ++e) g[b][e] = u[b][e] = 0.f;
-            if (i < items) {
-              for (int sp = 0; sp < p.splits; ++sp) {
-                const float4 a = red[((sp * kParts) * sg + gi[b]) * 128 + rl[b]];
-                g[b][0] += a.x;
-                g[b][1] += a.y;
-                g[b][2] += a.z;
-                g[b][3] += a.w;
-                if (kParts == 2) {
-                  const float4 c = red[((sp * kParts + 1) * sg + gi[b]) * 128 + rl[b]];
-                  u[b][0] += c.x;
-                  u[b][1] += c.y;
-                  u[b][2] += c.z;
-                  u[b][3] += c.w;
-                }
+            for (int j = 0; j < 4; ++j) {
+              const float4 a = __ldcg(src + (size_t)(c / 4 + j) * 128 + row_local);
+              pg[4 * j] = a.x;
+              pg[4 * j + 1] = a.y;
+              pg[4 * j + 2] = a.z;
+              pg[4 * j + 3] = a.w;
+              if (kNA == 2) {
+                const float4 b4 = __ldcg(src + (size_t)((p.bn + c) / 4 + j) * 128 + row_local);
+                pu[4 * j] = b4.x;
+                pu[4 * j + 1] = b4.y;
+                pu[4 * j + 2] = b4.z;
+                pu[4 * j + 3] = b4.w;
               }
             }
           }
 #pragma unroll
-          for (int b = 0; b < 4; ++b) {
-            const int i = i0 + b * kThreads;
-            const int row_b = m0 + rl[b];
-            if (i < items && ok && row_b < p.n_out)
-              epilogue_cols<EPI, 4>(p, n0 + c0 + cbase + 4 * gi[b], row_b, g[b], u[b]);
+          for (int j = 0; j < 16; ++j) {
+            g[j] = sp == 0 ? pg[j] : g[j] + pg[j];
+            if (kNA == 2) u[j] = sp == 0 ? pu[j] : u[j] + pu[j];
           }
         }
+        if (row_ok) epilogue_cols<EPI, 16>(p, n0 + c, row, g, u);
       }
-      cluster_sync();
     }
   }
   tc_fence_before();
@@ -551,31 +546,29 @@ TcPlan tc_plan(int n_tok, int n_out, int k, int epi) {
   pl.stages = (int)std::min<size_t>(8, kSmemBudget / stage);
   if (g_stages_option >= 2 && (size_t)g_stages_option * stage <= kSmemBudget) pl.stages = g_stages_option;
   pl.smem = (size_t)pl.stages * stage + 1024 + 256;
-  // split-K reduction pass width: the whole (64-rounded) tile if it fits the stage memory
-  auto red_need = [&](int cols) {
-    const int slice = ((cols + pl.splits - 1) / pl.splits + 15) / 16 * 16;
-    return (size_t)na * 128 * (size_t)slice * pl.splits * 4;
-  };
-  pl.red_cols = (pl.bn + 63) / 64 * 64;
-  while (pl.red_cols > 64 && red_need(pl.red_cols) > (size_t)pl.stages * stage) pl.red_cols -= 64;
-  pl.tmem_cols = next_pow2(na * pl.bn);
+  pl.acc_cols = na * pl.bn;
+  pl.tmem_cols = next_pow2(pl.acc_cols);
+  // split-K partial tiles: one fp32 tile per (output tile, token tile, split)
+  pl.partial_bytes = pl.splits > 1 ? (size_t)pl.out_tiles * pl.tok_tiles * pl.splits * 128 * (size_t)pl.acc_cols * 4 : 0;
   return pl;
+}
+
+size_t tc_partial_bytes_max(int max_tok, int n_out, int k, int epi) {
+  size_t b = 0;
+  for (int n = 1; n <= max_tok; ++n) b = std::max(b, tc_plan(n, n_out, k, epi).partial_bytes);
+  return b;
 }
 
 int tc_gemm_launch(int epi, const CUtensorMap& map_w, const void* x, int n_tok, int n_out, int k, int up_offset,
                    const void* residual, int ld_res, void* y, int ld_y, unsigned long long* keys, int* status,
-                   cudaStream_t stream, int a_packed) {
+                   cudaStream_t stream, int a_packed, const TcScratch& scratch) {
   if (a_packed && (k % kBK || up_offset % kBM)) return EESD_ERR_ARG;
   if (n_tok <= 0 || n_out <= 0 || k <= 0) return EESD_ERR_ARG;
   const TcPlan pl = tc_plan(n_tok, n_out, k, epi);
   if (pl.stages < 2) return EESD_ERR_ARG;
-  // the split-K reduction buffer lives in the (then idle) stage memory
-  {
-    const int na = epi == EESD_EPI_SWIGLU ? 2 : 1;
-    const int slice = ((pl.red_cols + pl.splits - 1) / pl.splits + 15) / 16 * 16;
-    const size_t red_bytes = (size_t)na * 128 * slice * pl.splits * 4;
-    if (pl.splits > 1 && red_bytes > (size_t)pl.stages * (na * kATileBytes + (size_t)pl.bn * kBK * 2)) return EESD_ERR_ARG;
-  }
+  if (pl.partial_bytes && (!scratch.partials || scratch.partial_bytes < pl.partial_bytes ||
+                           (reinterpret_cast<uintptr_t>(scratch.partials) & 15)))
+    return EESD_ERR_ARG;
   CUtensorMap map_x;
   int rc = encode_kmajor_map(&map_x, x, n_tok, k, pl.b_boxes == 2 ? pl.bn / 2 : pl.bn);
   if (rc) return rc;
@@ -593,7 +586,8 @@ int tc_gemm_launch(int epi, const CUtensorMap& map_w, const void* x, int n_tok, 
   p.up_offset = up_offset;
   p.tmem_cols = pl.tmem_cols;
   p.a_packed = a_packed;
-  p.red_cols = pl.red_cols;
+  p.acc_cols = pl.acc_cols;
+  p.partials = static_cast<float4*>(scratch.partials);
   p.residual = static_cast<const bf16*>(residual);
   p.ld_res = ld_res;
   p.y = static_cast<bf16*>(y);

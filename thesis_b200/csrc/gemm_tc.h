@@ -14,8 +14,15 @@ typedef CUresult (*PFN_encodeTiled_t)(CUtensorMap*, CUtensorMapDataType, cuuint3
                                       CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 struct TcPlan {
-  int tok_tiles, out_tiles, bn, b_boxes, mma_n, kb_total, kb_per, splits, stages, tmem_cols, red_cols;
+  int tok_tiles, out_tiles, bn, b_boxes, mma_n, kb_total, kb_per, splits, stages, acc_cols, tmem_cols;
   size_t smem;
+  size_t partial_bytes;   // split-K scratch the launch needs (0 without split)
+};
+
+// Global scratch of a split-K launch: fp32 partial tiles (16-byte aligned).
+struct TcScratch {
+  void* partials = nullptr;
+  size_t partial_bytes = 0;
 };
 
 PFN_encodeTiled_t tensor_map_encoder();
@@ -28,7 +35,9 @@ void tc_set_stages(int n);
 // a_packed = 1: map_w is a tile-packed weight map (encode_packed_map), else a row-major 2-D map
 int tc_gemm_launch(int epi, const CUtensorMap& map_w, const void* x, int n_tok, int n_out, int k, int up_offset,
                    const void* residual, int ld_res, void* y, int ld_y, unsigned long long* keys, int* status,
-                   cudaStream_t stream, int a_packed = 0);
+                   cudaStream_t stream, int a_packed, const TcScratch& scratch);
+// split-K scratch that covers every launch of this weight shape with 1..max_tok tokens
+size_t tc_partial_bytes_max(int max_tok, int n_out, int k, int epi);
 // Tile-packed weight layout: [ceil(rows/128) * (k/64) tiles][128 rows][64 cols], tile = row tile *
 // (k/64) + k-block, so every 128 x 64 operand tile is one contiguous 16 KB block (rows past the
 // end zero).  3-D map: {64, 128, tiles} with one tile per box and 128-byte swizzle.

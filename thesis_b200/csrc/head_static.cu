@@ -101,7 +101,8 @@ extern "C" int eesd_head_argmax_static(const void* x, const int32_t* rows, int n
     set_last_error("head_argmax_static: LM head tensor map (needs a 16-byte aligned bf16 [vocab, dim])");
     return rc;
   }
-  rc = tc_gemm_launch(EESD_EPI_ARGMAX_INTERNAL, map, xn, n, vocab, dim, 0, nullptr, 0, nullptr, 0, keys, status, s);
+  rc = tc_gemm_launch(EESD_EPI_ARGMAX_INTERNAL, map, xn, n, vocab, dim, 0, nullptr, 0, nullptr, 0, keys, status, s, 0,
+                      TcScratch{});  // the head is never split: no partial-tile scratch
   if (!rc) rc = launch_keys_to_ids(keys, out_ids, n, s);
   if (rc) set_last_error("head_argmax_static: head GEMM / argmax launch failed");
   return rc;

@@ -67,6 +67,7 @@ struct Model {
   float* gu;                    // fp32 path: [max_tokens, 2 I]
   float* logits32;              // fp32 path: [kHeadChunk, vocab]
   unsigned long long* keys;
+  TcScratch gemm_scratch;       // split-K partial tiles of the bf16 GEMM
   int64_t launches = 0;
   bool prof = false;
   std::vector<ProfEvent> events;
@@ -77,7 +78,7 @@ struct Model {
 constexpr int kHeadChunk = 128;
 
 struct Layout {
-  size_t status, xn, qkv, attn, act, gu, logits32, keys, total;
+  size_t status, xn, qkv, attn, act, gu, logits32, keys, partials, partial_bytes, total;
 };
 
 Layout layout_for(const EesdModelDesc& d) {
@@ -94,6 +95,17 @@ Layout layout_for(const EesdModelDesc& d) {
   L.gu = c.take(d.dtype == EESD_F32 ? T * 2 * d.intermediate * 4 : 0);
   L.logits32 = c.take(d.dtype == EESD_F32 ? (size_t)kHeadChunk * d.vocab * 4 : 0);
   L.keys = c.take(T * 8);
+  if (d.dtype == EESD_BF16) {
+    // split-K scratch that covers every projection at up to max_tokens tokens (the LM head is
+    // never split)
+    const int shapes[4][3] = {{qkv_dim, d.dim, EESD_EPI_STORE},
+                              {d.dim, q_dim, EESD_EPI_RESIDUAL},
+                              {d.intermediate, d.dim, EESD_EPI_SWIGLU},
+                              {d.dim, d.intermediate, EESD_EPI_RESIDUAL}};
+    for (const auto& sh : shapes)
+      L.partial_bytes = std::max(L.partial_bytes, tc_partial_bytes_max((int)T, sh[0], sh[1], sh[2]));
+  }
+  L.partials = c.take(L.partial_bytes);
   L.total = c.off;
   return L;
 }
@@ -125,7 +137,7 @@ int model_gemm(Model* m, int epi, const CUtensorMap& map, const void* w, const v
   const EesdModelDesc& d = m->d;
   if (d.dtype == EESD_BF16) {
     const int rc = tc_gemm_launch(epi, map, x, n_tok, n_out, k, up_offset, res, n_out, y, n_out, m->keys,
-                                  m->status, s, d.weights_packed);
+                                  m->status, s, d.weights_packed, m->gemm_scratch);
     m->launches += 1;
     return rc ? fail(rc, "tcgen05 gemm launch failed (n_tok=%d n_out=%d k=%d epi=%d)", n_tok, n_out, k, epi) : 0;
   }
@@ -211,6 +223,8 @@ int eesd_model_create(const EesdModelDesc* d, void** out) {
   m->gu = reinterpret_cast<float*>(ws + L.gu);
   m->logits32 = reinterpret_cast<float*>(ws + L.logits32);
   m->keys = reinterpret_cast<unsigned long long*>(ws + L.keys);
+  m->gemm_scratch.partials = ws + L.partials;
+  m->gemm_scratch.partial_bytes = L.partial_bytes;
   if (d->dtype == EESD_BF16) {
     m->map_qkv.resize(d->n_layers);
     m->map_o.resize(d->n_layers);
@@ -472,6 +486,7 @@ size_t eesd_gemm_workspace_bytes(int n_tok, int n_out, int k, int epilogue) {
   if (n_tok <= 0 || n_out <= 0 || k <= 0) return 0;
   size_t b = 256;                                                                  // status word
   if (epilogue == EESD_EPI_SWIGLU) b += align256((size_t)n_tok * 2 * n_out * 4);   // fp32 path scratch
+  if (k % 64 == 0) b += align256(tc_plan(n_tok, n_out, k, epilogue).partial_bytes);  // bf16 split-K scratch
   return b;
 }
 
@@ -490,11 +505,15 @@ int eesd_gemm(int dtype, int epilogue, const void* x, const void* w, const void*
   if (e != cudaSuccess) return cuda_fail(e, "gemm status reset");
   if (dtype == EESD_BF16) {
     if (k % 64) return fail(EESD_ERR_ARG, "bf16 gemm needs k %% 64 == 0");
+    TcScratch sc;
+    sc.partials = ws + 256 + (epilogue == EESD_EPI_SWIGLU ? align256((size_t)n_tok * 2 * n_out * 4) : 0);
+    sc.partial_bytes = tc_plan(n_tok, n_out, k, epilogue).partial_bytes;
     CUtensorMap map;
     const int rows = epilogue == EESD_EPI_SWIGLU ? up_offset + n_out : n_out;
     int rc = encode_kmajor_map(&map, w, rows, k, 128);
     if (rc) return fail(rc, "weight tensor map");
-    rc = tc_gemm_launch(epilogue, map, x, n_tok, n_out, k, up_offset, residual, n_out, y, n_out, nullptr, status, s);
+    rc = tc_gemm_launch(epilogue, map, x, n_tok, n_out, k, up_offset, residual, n_out, y, n_out, nullptr, status, s, 0,
+                        sc);
     return rc ? fail(rc, "tcgen05 gemm launch") : EESD_OK;
   }
   int rc;
