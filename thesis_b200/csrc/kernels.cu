@@ -287,7 +287,8 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(const __grid_constant__ 
                                                         const __grid_constant__ CUtensorMap vmap, AttnGeom g,
                                                         int item_tokens, int layer, const bf16* __restrict__ q,
                                                         bf16* __restrict__ out, const int32_t* __restrict__ blk,
-                                                        const int32_t* __restrict__ items, int* status) {
+                                                        const int32_t* __restrict__ items, int* status,
+                                                        AttnAppend app) {
   pdl_trigger();
   pdl_wait();
   constexpr int KT = 64;              // keys per tile
@@ -330,6 +331,9 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(const __grid_constant__ 
   }
   cp_async_commit();
   __syncthreads();
+  // With the in-kernel append, tiles below the first appended key are loaded while the append
+  // runs; the rest wait for it.
+  const int n_pre = app.on ? min(min(NS - 1, n_tiles), (pos0 + t0) / KT) : min(NS - 1, n_tiles);
   auto issue = [&](int tile) {
     const int s = tile % NS;
     const uint32_t fb = smem_u32(&full[s]);
@@ -344,7 +348,95 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(const __grid_constant__ 
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&kmap);
     tma_prefetch_desc(&vmap);
-    for (int t = 0; t < NS - 1 && t < n_tiles; ++t) issue(t);
+    for (int t = 0; t < n_pre; ++t) issue(t);
+  }
+  if (app.on) {
+    // RoPE (rotate-half, reference bf16 roundings as in the rope/KV kernel) for this item's tokens:
+    // k rotated and v copied into the cache first, then the proxy fence orders those generic
+    // stores before the TMA reads of the same key tiles; q is rotated in shared memory.
+    const int half = D / 2;
+    const bool valid = row >= 0 && row < g.max_batch && pos0 >= 0 && pos0 + t0 + nt <= g.max_seq;
+    if (!valid) {
+      if (threadIdx.x == 0) set_status(status, kStatusBadIndex);
+    } else {
+      bf16* kc = static_cast<bf16*>(app.kc) + ((size_t)row * g.n_kv_heads + kvh) * g.max_seq * D;
+      bf16* vc = static_cast<bf16*>(app.vc) + ((size_t)row * g.n_kv_heads + kvh) * g.max_seq * D;
+      constexpr int kU = 4;   // independent (token, pair) items per thread in flight
+      for (int i0 = threadIdx.x; i0 < nt * half; i0 += kU * 128) {
+        float x1[kU], x2[kU], c1[kU], c2[kU], s1[kU], s2[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const int i = i0 + u * 128;
+          if (i < nt * half) {
+            const int tt = i / half, d = i - tt * half, pos = pos0 + t0 + tt;
+            const bf16* src = q + (size_t)(start + t0 + tt) * g.ld_q + (g.n_heads + kvh) * D;
+            x1[u] = __bfloat162float(__ldg(src + d));
+            x2[u] = __bfloat162float(__ldg(src + d + half));
+            c1[u] = __ldg(app.cos + (size_t)pos * D + d);
+            c2[u] = __ldg(app.cos + (size_t)pos * D + d + half);
+            s1[u] = __ldg(app.sin + (size_t)pos * D + d);
+            s2[u] = __ldg(app.sin + (size_t)pos * D + d + half);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const int i = i0 + u * 128;
+          if (i < nt * half) {
+            const int tt = i / half, d = i - tt * half, pos = pos0 + t0 + tt;
+            const float k1 = rnd<bf16>(x1[u] * rnd<bf16>(c1[u])) + rnd<bf16>(-x2[u] * rnd<bf16>(s1[u]));
+            const float k2 = rnd<bf16>(x2[u] * rnd<bf16>(c2[u])) + rnd<bf16>(x1[u] * rnd<bf16>(s2[u]));
+            kc[(size_t)pos * D + d] = __float2bfloat16_rn(k1);
+            kc[(size_t)pos * D + d + half] = __float2bfloat16_rn(k2);
+          }
+        }
+      }
+      for (int i = threadIdx.x; i < nt * (D / 8); i += 128) {
+        const int tt = i / (D / 8), c8 = i - tt * (D / 8), pos = pos0 + t0 + tt;
+        const uint4* src = reinterpret_cast<const uint4*>(q + (size_t)(start + t0 + tt) * g.ld_q +
+                                                          (g.n_heads + g.n_kv_heads + kvh) * D) + c8;
+        reinterpret_cast<uint4*>(vc + (size_t)pos * D)[c8] = *src;
+      }
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+    }
+    cp_async_wait<0>();
+    __syncthreads();
+    if (valid) {
+      // thread -> rotation pair d of one token group; the G rows of a token share cos / sin
+      const int groups = 128 / half;
+      const int d = threadIdx.x % half;
+      constexpr int kU = 4;
+      for (int tt0 = threadIdx.x / half; tt0 < nt; tt0 += kU * groups) {
+        float c1[kU], c2[kU], s1[kU], s2[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const int tt = tt0 + u * groups;
+          if (tt < nt) {
+            const int pos = pos0 + t0 + tt;
+            c1[u] = __ldg(app.cos + (size_t)pos * D + d);
+            c2[u] = __ldg(app.cos + (size_t)pos * D + d + half);
+            s1[u] = __ldg(app.sin + (size_t)pos * D + d);
+            s2[u] = __ldg(app.sin + (size_t)pos * D + d + half);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const int tt = tt0 + u * groups;
+          if (tt < nt) {
+            const float cc1 = rnd<bf16>(c1[u]), cc2 = rnd<bf16>(c2[u]), ss1 = rnd<bf16>(s1[u]), ss2 = rnd<bf16>(s2[u]);
+            for (int gh = 0; gh < G; ++gh) {
+              bf16* qr = Qs + (tt * G + gh) * LDQ;
+              const float x1 = __bfloat162float(qr[d]), x2 = __bfloat162float(qr[d + half]);
+              qr[d] = __float2bfloat16_rn(rnd<bf16>(x1 * cc1) + rnd<bf16>(-x2 * ss1));
+              qr[d + half] = __float2bfloat16_rn(rnd<bf16>(x2 * cc2) + rnd<bf16>(x1 * ss2));
+            }
+          }
+        }
+      }
+    }
+    __syncthreads();
+    // the tiles holding the appended keys go out only now
+    if (threadIdx.x == 0)
+      for (int t = n_pre; t < NS - 1 && t < n_tiles; ++t) issue(t);
   }
   cp_async_wait<0>();
   __syncthreads();
@@ -703,8 +795,9 @@ int launch_rope_kv(int dtype, void* qkv, const int32_t* tok_pos, const int32_t* 
 
 int launch_attention(int dtype, const AttnGeom& g, const void* q, const void* kc, const void* vc, void* out,
                      const int32_t* blk, const int32_t* items, int n_items, int max_ctx, int* status, cudaStream_t s,
-                     const CUtensorMap* kmap, const CUtensorMap* vmap, int layer) {
+                     const CUtensorMap* kmap, const CUtensorMap* vmap, int layer, const AttnAppend& app) {
   (void)max_ctx;
+  if (app.on && (dtype != EESD_BF16 || !app.kc || !app.vc || !app.cos || !app.sin)) return EESD_ERR_ARG;
   if (n_items <= 0) return EESD_OK;
   const int it = attn_item_tokens(g.n_heads, g.n_kv_heads);
   dim3 grid(n_items, g.n_kv_heads);
@@ -719,7 +812,7 @@ int launch_attention(int dtype, const AttnGeom& g, const void* q, const void* kc
         set = true;
       }
       launch_pdl(attn_bf16_kernel<128>, dim3(grid), dim3(128), sm, s, *kmap, *vmap, g, it, layer, (const bf16*)q, (bf16*)out, blk, items,
-                                                  status);
+                                                  status, app);
     } else if (g.head_dim == 64) {
       const size_t sm = 1024 + 3 * (2 * 1 * 64 * 128) + 32 * (64 + 8) * 2 + 64;
       static bool set = false;
@@ -729,7 +822,7 @@ int launch_attention(int dtype, const AttnGeom& g, const void* q, const void* kc
         set = true;
       }
       launch_pdl(attn_bf16_kernel<64>, dim3(grid), dim3(128), sm, s, *kmap, *vmap, g, it, layer, (const bf16*)q, (bf16*)out, blk, items,
-                                                 status);
+                                                 status, app);
     } else {
       return EESD_ERR_ARG;
     }

@@ -23,11 +23,22 @@ int launch_rmsnorm(int dtype, const void* x, const int32_t* rows, const void* w,
 int launch_rope_kv(int dtype, void* qkv, const int32_t* tok_pos, const int32_t* tok_row, int n_tok, int n_heads,
                    int n_kv_heads, int head_dim, const float* cos, const float* sin, void* kc, void* vc, int max_batch,
                    int max_seq, int* status, cudaStream_t s);
+// RoPE + KV append done by the bf16 attention kernel itself (every block of the batch must fit
+// one work item, so the CTA that appends a block's keys is the only one that reads them):
+// q, k, v are read unrotated from the fused projection, q rotated in shared memory, k rotated
+// and v copied into this layer's caches kc / vc ([max_batch, Hkv, max_seq, D]).
+struct AttnAppend {
+  bool on = false;
+  void* kc = nullptr;
+  void* vc = nullptr;
+  const float* cos = nullptr;   // [max_seq, D]
+  const float* sin = nullptr;
+};
 // kc / vc: the whole cache [n_layers, max_batch, Hkv, max_seq, D]; bf16 reads it through the
 // 2-D TMA maps kmap / vmap ([n_layers * max_batch * Hkv * max_seq, D], 64 x 64 boxes, 128B swizzle)
 int launch_attention(int dtype, const AttnGeom& g, const void* q, const void* kc, const void* vc, void* out,
                      const int32_t* blk, const int32_t* items, int n_items, int max_ctx, int* status, cudaStream_t s,
-                     const CUtensorMap* kmap, const CUtensorMap* vmap, int layer);
+                     const CUtensorMap* kmap, const CUtensorMap* vmap, int layer, const AttnAppend& app = AttnAppend());
 int launch_embed(int dtype, const void* table, const int32_t* ids, int n, int dim, int vocab, void* x, int* status,
                  cudaStream_t s);
 int launch_copy_rows(int dtype, const void* src, const int32_t* src_idx, void* dst, const int32_t* dst_idx, int n,

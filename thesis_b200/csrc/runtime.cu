@@ -303,15 +303,26 @@ int eesd_forward_layers(void* h, void* x, const EesdBatch* b, int start, int end
                     m->qkv_dim, d.dim, 0, nullptr, m->qkv, s);
     prof_end(m, s, &pe);
     if (rc) return rc;
-    prof_begin(m, s, EESD_PROF_ROPE_KV, &pe, N);
-    rc = launch_rope_kv(d.dtype, m->qkv, b->tok_pos, b->tok_row, N, d.n_heads, d.n_kv_heads, d.head_dim, d.rope_cos,
-                        d.rope_sin, kc, vc, d.max_batch, d.max_seq, m->status, s);
-    prof_end(m, s, &pe);
-    m->launches++;
-    if (rc) return fail(rc, "rope/kv launch");
+    // Draft and verify batches (every block one attention work item): the attention kernel does
+    // RoPE and the KV append itself.  Batches with longer blocks (prefill) use the RoPE/KV kernel.
+    AttnAppend app;
+    app.on = d.dtype == EESD_BF16 && b->n_items == b->n_blocks;
+    if (app.on) {
+      app.kc = kc;
+      app.vc = vc;
+      app.cos = d.rope_cos;
+      app.sin = d.rope_sin;
+    } else {
+      prof_begin(m, s, EESD_PROF_ROPE_KV, &pe, N);
+      rc = launch_rope_kv(d.dtype, m->qkv, b->tok_pos, b->tok_row, N, d.n_heads, d.n_kv_heads, d.head_dim, d.rope_cos,
+                          d.rope_sin, kc, vc, d.max_batch, d.max_seq, m->status, s);
+      prof_end(m, s, &pe);
+      m->launches++;
+      if (rc) return fail(rc, "rope/kv launch");
+    }
     prof_begin(m, s, EESD_PROF_ATTN, &pe, N);
     rc = launch_attention(d.dtype, g, m->qkv, d.k_cache, d.v_cache, m->attn, b->blk, b->items, b->n_items, b->max_ctx,
-                          m->status, s, &m->map_kc, &m->map_vc, i);
+                          m->status, s, &m->map_kc, &m->map_vc, i, app);
     prof_end(m, s, &pe);
     m->launches++;
     if (rc) return fail(rc, "attention launch");
