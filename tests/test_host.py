@@ -22,8 +22,11 @@ def test_packing_metadata():
         assert set(ph.tok_row[sl]) == {r}
         assert tuple(ph.blk[i]) == (ph.offsets[i], T, r, p0)
     # the 40-token block is tiled into items of 16 query tokens: 0, 16, 32
-    assert [tuple(x) for x in ph.items if x[0] == 2] == [(2, 0), (2, 16), (2, 32)]
+    assert sorted(tuple(x) for x in ph.items if x[0] == 2) == [(2, 0), (2, 16), (2, 32)]
     assert len(ph.items) == 6
+    # items are ordered longest key range (pos0 + last query token + 1) first
+    kv = [int(ph.blk[b][3]) + min(int(t0) + 16, int(ph.blk[b][1])) for b, t0 in ph.items]
+    assert kv == sorted(kv, reverse=True) and kv[0] == 47
     assert ph.max_ctx == 47 and ph.kv_read == 13 + 6 + 47 + 10
     with pytest.raises(ValueError):
         pack([(0, 0, 0)], 16)

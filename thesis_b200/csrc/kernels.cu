@@ -276,14 +276,15 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
-// Item rows <= 32 (two 16-row groups).  K/V tiles of 64 keys arrive by TMA (one thread issues
-// them into a 3-stage mbarrier ring; 128-byte swizzled 64-dim halves).  The 4 warps split every
-// tile by absolute key position (warp w takes keys 16w .. 16w+15) and keep their own running
-// max, sum and output for every row; the four partial states are merged in warp order at the
-// end.  A row's arithmetic therefore depends only on its own query, its keys and the fixed key
-// partition, never on the other rows of the launch.
-template <int D>
-__global__ void __launch_bounds__(128) attn_bf16_kernel(const __grid_constant__ CUtensorMap kmap,
+// Item rows <= 16 * WARPS / 4 (16-row groups).  K/V tiles of 64 keys arrive by TMA (one thread
+// issues them into an NS-stage mbarrier ring; 128-byte swizzled 64-dim halves).  Warp w owns row
+// group w / 4 and key quarter w % 4: it takes keys 16 (w % 4) .. +15 of every tile and keeps its
+// own running max, sum and output for its rows; the four quarters' states are merged in quarter
+// order at the end.  A row's arithmetic therefore depends only on its own query, its keys and the
+// fixed key partition, never on the other rows of the launch or on WARPS (4 warps for one row
+// group: draft steps; 8 for two: verify steps).
+template <int D, int WARPS, int NS, int MINB>
+__global__ void __launch_bounds__(WARPS * 32, MINB) attn_bf16_kernel(const __grid_constant__ CUtensorMap kmap,
                                                         const __grid_constant__ CUtensorMap vmap, AttnGeom g,
                                                         int item_tokens, int layer, const bf16* __restrict__ q,
                                                         bf16* __restrict__ out, const int32_t* __restrict__ blk,
@@ -292,7 +293,8 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(const __grid_constant__ 
   pdl_trigger();
   pdl_wait();
   constexpr int KT = 64;              // keys per tile
-  constexpr int NS = 3;               // TMA stages
+  constexpr int NT = WARPS * 32;      // threads
+  constexpr int RMAX = 16 * (WARPS / 4);   // query rows per item
   constexpr int HALVES = D / 64;      // 64-dim swizzled sub-tiles per K (or V) tile
   constexpr uint32_t SUB = KT * 128;  // bytes of one sub-tile (64 keys x 128 B)
   constexpr uint32_t STAGE = 2 * HALVES * SUB;
@@ -302,8 +304,8 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(const __grid_constant__ 
   extern __shared__ __align__(16) uint8_t smem8[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem8) + 1023) & ~uintptr_t(1023));
   uint8_t* stages = sm;                                            // [NS][K halves | V halves]
-  bf16* Qs = reinterpret_cast<bf16*>(sm + NS * STAGE);             // [32][LDQ]
-  uint64_t* full = reinterpret_cast<uint64_t*>(Qs + 32 * LDQ);     // [NS]
+  bf16* Qs = reinterpret_cast<bf16*>(sm + NS * STAGE);             // [RMAX][LDQ]
+  uint64_t* full = reinterpret_cast<uint64_t*>(Qs + RMAX * LDQ);   // [NS]
   volatile int* abort_flag = reinterpret_cast<volatile int*>(full + NS);
 
   const int item = blockIdx.x, kvh = blockIdx.y;
@@ -311,7 +313,7 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(const __grid_constant__ 
   const int start = blk[4 * b], T = blk[4 * b + 1], row = blk[4 * b + 2], pos0 = blk[4 * b + 3];
   const int G = g.n_heads / g.n_kv_heads;
   const int nt = min(item_tokens, T - t0);
-  const int nrows = nt * G;                             // <= 32
+  const int nrows = min(nt * G, RMAX);                  // the launcher picks RMAX >= nt * G
   const int kv_len = pos0 + t0 + nt;
   const int n_tiles = (kv_len + KT - 1) / KT;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -323,7 +325,7 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(const __grid_constant__ 
     *abort_flag = 0;
     fence_mbar_init();
   }
-  for (int c = threadIdx.x; c < 32 * CPR; c += 128) {
+  for (int c = threadIdx.x; c < RMAX * CPR; c += NT) {
     const int r = c / CPR, cc = c - r * CPR;
     const bool in = r < nrows;
     const bf16* src = in ? q + (size_t)(start + t0 + r / G) * g.ld_q + (kvh * G + r % G) * D + cc * 8 : q;
@@ -362,11 +364,11 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(const __grid_constant__ 
       bf16* kc = static_cast<bf16*>(app.kc) + ((size_t)row * g.n_kv_heads + kvh) * g.max_seq * D;
       bf16* vc = static_cast<bf16*>(app.vc) + ((size_t)row * g.n_kv_heads + kvh) * g.max_seq * D;
       constexpr int kU = 4;   // independent (token, pair) items per thread in flight
-      for (int i0 = threadIdx.x; i0 < nt * half; i0 += kU * 128) {
+      for (int i0 = threadIdx.x; i0 < nt * half; i0 += kU * NT) {
         float x1[kU], x2[kU], c1[kU], c2[kU], s1[kU], s2[kU];
 #pragma unroll
         for (int u = 0; u < kU; ++u) {
-          const int i = i0 + u * 128;
+          const int i = i0 + u * NT;
           if (i < nt * half) {
             const int tt = i / half, d = i - tt * half, pos = pos0 + t0 + tt;
             const bf16* src = q + (size_t)(start + t0 + tt) * g.ld_q + (g.n_heads + kvh) * D;
@@ -380,7 +382,7 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(const __grid_constant__ 
         }
 #pragma unroll
         for (int u = 0; u < kU; ++u) {
-          const int i = i0 + u * 128;
+          const int i = i0 + u * NT;
           if (i < nt * half) {
             const int tt = i / half, d = i - tt * half, pos = pos0 + t0 + tt;
             const float k1 = rnd<bf16>(x1[u] * rnd<bf16>(c1[u])) + rnd<bf16>(-x2[u] * rnd<bf16>(s1[u]));
@@ -390,7 +392,7 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(const __grid_constant__ 
           }
         }
       }
-      for (int i = threadIdx.x; i < nt * (D / 8); i += 128) {
+      for (int i = threadIdx.x; i < nt * (D / 8); i += NT) {
         const int tt = i / (D / 8), c8 = i - tt * (D / 8), pos = pos0 + t0 + tt;
         const uint4* src = reinterpret_cast<const uint4*>(q + (size_t)(start + t0 + tt) * g.ld_q +
                                                           (g.n_heads + g.n_kv_heads + kvh) * D) + c8;
@@ -402,7 +404,7 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(const __grid_constant__ 
     __syncthreads();
     if (valid) {
       // thread -> rotation pair d of one token group; the G rows of a token share cos / sin
-      const int groups = 128 / half;
+      const int groups = NT / half;
       const int d = threadIdx.x % half;
       constexpr int kU = 4;
       for (int tt0 = threadIdx.x / half; tt0 < nt; tt0 += kU * groups) {
@@ -442,24 +444,22 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(const __grid_constant__ 
   __syncthreads();
 
   const int gq = lane >> 2, tq = lane & 3;
-  const int n_rg = (nrows + 15) / 16;                   // 1 or 2 row groups
-  int qpos[2][2];
-#pragma unroll
-  for (int rg = 0; rg < 2; ++rg) {
+  const int n_rg = (nrows + 15) / 16;                   // row groups with rows
+  const int rg = warp >> 2;                             // this warp's row group
+  const int kq = warp & 3;                              // this warp's key quarter
+  int qpos[2];
+  {
     const int r0 = rg * 16 + gq, r1 = r0 + 8;
-    qpos[rg][0] = r0 < nrows ? pos0 + t0 + r0 / G : -1;
-    qpos[rg][1] = r1 < nrows ? pos0 + t0 + r1 / G : -1;
+    qpos[0] = r0 < nrows ? pos0 + t0 + r0 / G : -1;
+    qpos[1] = r1 < nrows ? pos0 + t0 + r1 / G : -1;
   }
-  float o[2][ND][4];
-  float m[2][2], l[2][2];
+  float o[ND][4];
+  float m[2], l[2];
+  m[0] = m[1] = -INFINITY;
+  l[0] = l[1] = 0.f;
 #pragma unroll
-  for (int rg = 0; rg < 2; ++rg) {
-    m[rg][0] = m[rg][1] = -INFINITY;
-    l[rg][0] = l[rg][1] = 0.f;
-#pragma unroll
-    for (int n = 0; n < ND; ++n) o[rg][n][0] = o[rg][n][1] = o[rg][n][2] = o[rg][n][3] = 0.f;
-  }
-  const int kw = warp * 16;                             // this warp's keys inside every tile
+  for (int n = 0; n < ND; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  const int kw = kq * 16;                               // this warp's keys inside every tile
   const float scale_l2 = g.scale * 1.4426950408889634f;  // softmax scale times log2(e)
 
   for (int tile = 0; tile < n_tiles; ++tile) {
@@ -470,8 +470,7 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(const __grid_constant__ 
     }
     const uint32_t kt = smem_u32(stages + (tile % NS) * STAGE);
     const uint32_t vt = kt + HALVES * SUB;
-#pragma unroll
-    for (int rg = 0; rg < 2; ++rg) {
+    {
       if (rg < n_rg) {
         float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
@@ -498,8 +497,8 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(const __grid_constant__ 
             s[n][2 + e] *= scale_l2;
             if (need_mask) {
               const int key = kbase + n * 8 + e;
-              if (key > qpos[rg][0]) s[n][e] = -INFINITY;
-              if (key > qpos[rg][1]) s[n][2 + e] = -INFINITY;
+              if (key > qpos[0]) s[n][e] = -INFINITY;
+              if (key > qpos[1]) s[n][2 + e] = -INFINITY;
             }
             mx0 = fmaxf(mx0, s[n][e]);
             mx1 = fmaxf(mx1, s[n][2 + e]);
@@ -509,13 +508,13 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(const __grid_constant__ 
         mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
         mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
         mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-        const float mn0 = fmaxf(m[rg][0], mx0), mn1 = fmaxf(m[rg][1], mx1);
+        const float mn0 = fmaxf(m[0], mx0), mn1 = fmaxf(m[1], mx1);
         // the running output needs rescaling only when some row's maximum moved
-        const bool moved = !__all_sync(0xffffffffu, mn0 == m[rg][0] && mn1 == m[rg][1]);
+        const bool moved = !__all_sync(0xffffffffu, mn0 == m[0] && mn1 == m[1]);
         const float ms0 = mn0 == -INFINITY ? 0.f : mn0, ms1 = mn1 == -INFINITY ? 0.f : mn1;
-        const float c0 = fast_exp2(m[rg][0] - ms0), c1 = fast_exp2(m[rg][1] - ms1);
-        m[rg][0] = mn0;
-        m[rg][1] = mn1;
+        const float c0 = fast_exp2(m[0] - ms0), c1 = fast_exp2(m[1] - ms1);
+        m[0] = mn0;
+        m[1] = mn1;
         float ps0 = 0.f, ps1 = 0.f;
 #pragma unroll
         for (int n = 0; n < 2; ++n) {
@@ -527,17 +526,17 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(const __grid_constant__ 
             ps1 += s[n][2 + e];
           }
         }
-        l[rg][0] = l[rg][0] * c0 + ps0;
-        l[rg][1] = l[rg][1] * c1 + ps1;
+        l[0] = l[0] * c0 + ps0;
+        l[1] = l[1] * c1 + ps1;
         const uint32_t p0 = pack_bf16(s[0][0], s[0][1]), p1 = pack_bf16(s[0][2], s[0][3]);
         const uint32_t p2 = pack_bf16(s[1][0], s[1][1]), p3 = pack_bf16(s[1][2], s[1][3]);
         if (moved) {
 #pragma unroll
           for (int n = 0; n < ND; ++n) {
-            o[rg][n][0] *= c0;
-            o[rg][n][1] *= c0;
-            o[rg][n][2] *= c1;
-            o[rg][n][3] *= c1;
+            o[n][0] *= c0;
+            o[n][1] *= c0;
+            o[n][2] *= c1;
+            o[n][3] *= c1;
           }
         }
 #pragma unroll
@@ -547,55 +546,53 @@ __global__ void __launch_bounds__(128) attn_bf16_kernel(const __grid_constant__ 
           const uint32_t chunk = (uint32_t)((dim & 63) >> 3) ^ (uint32_t)(key & 7);
           uint32_t b0, b1, b2, b3;
           ldsm_x4_t(vt + (dim >> 6) * SUB + key * 128 + chunk * 16, b0, b1, b2, b3);
-          mma_bf16(o[rg][n2], p0, p1, p2, p3, b0, b1);
-          mma_bf16(o[rg][n2 + 1], p0, p1, p2, p3, b2, b3);
+          mma_bf16(o[n2], p0, p1, p2, p3, b0, b1);
+          mma_bf16(o[n2 + 1], p0, p1, p2, p3, b2, b3);
         }
       }
     }
     __syncthreads();
   }
-  // ---- merge the four warps' partial states in warp order (stage memory is free now)
+  // ---- merge the four key quarters' partial states in quarter order (stage memory is free now)
   constexpr int OLD = D + 4;
-  float* Ms = reinterpret_cast<float*>(stages);          // [4][32]
-  float* Lw = Ms + 4 * 32;                               // [4][32]
-  float* Ow = Lw + 4 * 32;                               // [4][32][OLD]
+  float* Ms = reinterpret_cast<float*>(stages);          // [4][RMAX]
+  float* Lw = Ms + 4 * RMAX;                             // [4][RMAX]
+  float* Ow = Lw + 4 * RMAX;                             // [4][RMAX][OLD]
+  static_assert((8 * RMAX + 4 * RMAX * (D + 4)) * 4 <= NS * STAGE, "merge buffers exceed the stage memory");
+  if (rg < n_rg) {
+    float l0 = l[0], l1 = l[1];
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+    const int r0 = rg * 16 + gq, r1 = r0 + 8;
+    if (tq == 0) {
+      Ms[kq * RMAX + r0] = m[0];
+      Ms[kq * RMAX + r1] = m[1];
+      Lw[kq * RMAX + r0] = l0;
+      Lw[kq * RMAX + r1] = l1;
+    }
 #pragma unroll
-  for (int rg = 0; rg < 2; ++rg) {
-    if (rg < n_rg) {
-      float l0 = l[rg][0], l1 = l[rg][1];
-      l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
-      l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
-      l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
-      l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-      const int r0 = rg * 16 + gq, r1 = r0 + 8;
-      if (tq == 0) {
-        Ms[warp * 32 + r0] = m[rg][0];
-        Ms[warp * 32 + r1] = m[rg][1];
-        Lw[warp * 32 + r0] = l0;
-        Lw[warp * 32 + r1] = l1;
-      }
-#pragma unroll
-      for (int n = 0; n < ND; ++n) {
-        const int d = n * 8 + 2 * tq;
-        *reinterpret_cast<float2*>(&Ow[(warp * 32 + r0) * OLD + d]) = make_float2(o[rg][n][0], o[rg][n][1]);
-        *reinterpret_cast<float2*>(&Ow[(warp * 32 + r1) * OLD + d]) = make_float2(o[rg][n][2], o[rg][n][3]);
-      }
+    for (int n = 0; n < ND; ++n) {
+      const int d = n * 8 + 2 * tq;
+      *reinterpret_cast<float2*>(&Ow[(kq * RMAX + r0) * OLD + d]) = make_float2(o[n][0], o[n][1]);
+      *reinterpret_cast<float2*>(&Ow[(kq * RMAX + r1) * OLD + d]) = make_float2(o[n][2], o[n][3]);
     }
   }
   __syncthreads();
   const int hd = g.n_heads * D;
-  for (int idx = threadIdx.x; idx < nrows * (D / 2); idx += 128) {
+  for (int idx = threadIdx.x; idx < nrows * (D / 2); idx += NT) {
     const int r = idx / (D / 2), d = (idx - r * (D / 2)) * 2;
     float mx = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < 4; ++w) mx = fmaxf(mx, Ms[w * 32 + r]);
+    for (int w = 0; w < 4; ++w) mx = fmaxf(mx, Ms[w * RMAX + r]);
     float lsum = 0.f, a = 0.f, bsum = 0.f;
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
-      const float mw = Ms[w * 32 + r];
+      const float mw = Ms[w * RMAX + r];
       const float f = mw == -INFINITY ? 0.f : fast_exp2(mw - mx);
-      const float2 ov = *reinterpret_cast<const float2*>(&Ow[(w * 32 + r) * OLD + d]);
-      lsum += Lw[w * 32 + r] * f;
+      const float2 ov = *reinterpret_cast<const float2*>(&Ow[(w * RMAX + r) * OLD + d]);
+      lsum += Lw[w * RMAX + r] * f;
       a += ov.x * f;
       bsum += ov.y * f;
     }
@@ -793,9 +790,28 @@ int launch_rope_kv(int dtype, void* qkv, const int32_t* tok_pos, const int32_t* 
   return launched();
 }
 
+template <int D, int WARPS, int NS, int MINB>
+int launch_attn_variant(dim3 grid, cudaStream_t s, const CUtensorMap& kmap, const CUtensorMap& vmap, const AttnGeom& g,
+                        int it, int layer, const void* q, void* out, const int32_t* blk, const int32_t* items,
+                        int* status, const AttnAppend& app) {
+  constexpr int RMAX = 16 * (WARPS / 4);
+  const size_t sm = 1024 + (size_t)NS * (2 * (D / 64) * 64 * 128) + (size_t)RMAX * (D + 8) * 2 + 64;
+  static bool set = false;
+  if (!set) {
+    if (cudaFuncSetAttribute(attn_bf16_kernel<D, WARPS, NS, MINB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)sm))
+      return EESD_ERR_CUDA;
+    set = true;
+  }
+  launch_pdl(attn_bf16_kernel<D, WARPS, NS, MINB>, grid, dim3(WARPS * 32), sm, s, kmap, vmap, g, it, layer,
+             (const bf16*)q, (bf16*)out, blk, items, status, app);
+  return EESD_OK;
+}
+
 int launch_attention(int dtype, const AttnGeom& g, const void* q, const void* kc, const void* vc, void* out,
                      const int32_t* blk, const int32_t* items, int n_items, int max_ctx, int* status, cudaStream_t s,
-                     const CUtensorMap* kmap, const CUtensorMap* vmap, int layer, const AttnAppend& app) {
+                     const CUtensorMap* kmap, const CUtensorMap* vmap, int layer, const AttnAppend& app,
+                     int rows_max) {
   (void)max_ctx;
   if (app.on && (dtype != EESD_BF16 || !app.kc || !app.vc || !app.cos || !app.sin)) return EESD_ERR_ARG;
   if (n_items <= 0) return EESD_OK;
@@ -803,29 +819,18 @@ int launch_attention(int dtype, const AttnGeom& g, const void* q, const void* kc
   dim3 grid(n_items, g.n_kv_heads);
   if (dtype == EESD_BF16) {
     if (!kmap || !vmap) return EESD_ERR_ARG;
-    if (g.head_dim == 128) {
-      const size_t sm = 1024 + 3 * (2 * 2 * 64 * 128) + 32 * (128 + 8) * 2 + 64;
-      static bool set = false;
-      if (!set) {
-        if (cudaFuncSetAttribute(attn_bf16_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm))
-          return EESD_ERR_CUDA;
-        set = true;
-      }
-      launch_pdl(attn_bf16_kernel<128>, dim3(grid), dim3(128), sm, s, *kmap, *vmap, g, it, layer, (const bf16*)q, (bf16*)out, blk, items,
-                                                  status, app);
-    } else if (g.head_dim == 64) {
-      const size_t sm = 1024 + 3 * (2 * 1 * 64 * 128) + 32 * (64 + 8) * 2 + 64;
-      static bool set = false;
-      if (!set) {
-        if (cudaFuncSetAttribute(attn_bf16_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm))
-          return EESD_ERR_CUDA;
-        set = true;
-      }
-      launch_pdl(attn_bf16_kernel<64>, dim3(grid), dim3(128), sm, s, *kmap, *vmap, g, it, layer, (const bf16*)q, (bf16*)out, blk, items,
-                                                 status, app);
-    } else {
+    // rows per item <= 16: 4 warps, 2 stages, 3 CTAs per SM; else 8 warps, 3 stages, 2 per SM
+    const bool small = rows_max <= 16;
+    int rc;
+    if (g.head_dim == 128)
+      rc = small ? launch_attn_variant<128, 4, 2, 3>(grid, s, *kmap, *vmap, g, it, layer, q, out, blk, items, status, app)
+                 : launch_attn_variant<128, 8, 3, 2>(grid, s, *kmap, *vmap, g, it, layer, q, out, blk, items, status, app);
+    else if (g.head_dim == 64)
+      rc = small ? launch_attn_variant<64, 4, 2, 3>(grid, s, *kmap, *vmap, g, it, layer, q, out, blk, items, status, app)
+                 : launch_attn_variant<64, 8, 3, 2>(grid, s, *kmap, *vmap, g, it, layer, q, out, blk, items, status, app);
+    else
       return EESD_ERR_ARG;
-    }
+    if (rc) return rc;
   } else {
     const size_t layer_off = (size_t)g.max_batch * g.n_kv_heads * g.max_seq * g.head_dim * (size_t)layer;
     const float* kl = static_cast<const float*>(kc) + layer_off;

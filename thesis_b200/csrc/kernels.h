@@ -38,7 +38,8 @@ struct AttnAppend {
 // 2-D TMA maps kmap / vmap ([n_layers * max_batch * Hkv * max_seq, D], 64 x 64 boxes, 128B swizzle)
 int launch_attention(int dtype, const AttnGeom& g, const void* q, const void* kc, const void* vc, void* out,
                      const int32_t* blk, const int32_t* items, int n_items, int max_ctx, int* status, cudaStream_t s,
-                     const CUtensorMap* kmap, const CUtensorMap* vmap, int layer, const AttnAppend& app = AttnAppend());
+                     const CUtensorMap* kmap, const CUtensorMap* vmap, int layer, const AttnAppend& app = AttnAppend(),
+                     int rows_max = 32);   // rows_max: largest item's query rows (tokens x GQA group)
 int launch_embed(int dtype, const void* table, const int32_t* ids, int n, int dim, int vocab, void* x, int* status,
                  cudaStream_t s);
 int launch_copy_rows(int dtype, const void* src, const int32_t* src_idx, void* dst, const int32_t* dst_idx, int n,

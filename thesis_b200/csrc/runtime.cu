@@ -290,6 +290,9 @@ int eesd_forward_layers(void* h, void* x, const EesdBatch* b, int start, int end
   AttnGeom g{d.n_heads, d.n_kv_heads, d.head_dim, d.max_batch, d.max_seq, m->qkv_dim,
              1.0f / sqrtf((float)d.head_dim)};
   ProfEvent pe;
+  // query rows of the largest attention work item: one token per block (draft) or up to a full item
+  const int G = d.n_heads / d.n_kv_heads;
+  const int rows_max = b->n_tokens == b->n_blocks ? G : attn_item_tokens(d.n_heads, d.n_kv_heads) * G;
   for (int i = start; i < end; ++i) {
     uint8_t* kc = static_cast<uint8_t*>(d.k_cache) + (size_t)i * layer_kv;
     uint8_t* vc = static_cast<uint8_t*>(d.v_cache) + (size_t)i * layer_kv;
@@ -322,7 +325,7 @@ int eesd_forward_layers(void* h, void* x, const EesdBatch* b, int start, int end
     }
     prof_begin(m, s, EESD_PROF_ATTN, &pe, N);
     rc = launch_attention(d.dtype, g, m->qkv, d.k_cache, d.v_cache, m->attn, b->blk, b->items, b->n_items, b->max_ctx,
-                          m->status, s, &m->map_kc, &m->map_vc, i, app);
+                          m->status, s, &m->map_kc, &m->map_vc, i, app, rows_max);
     prof_end(m, s, &pe);
     m->launches++;
     if (rc) return fail(rc, "attention launch");

@@ -69,6 +69,9 @@ def pack(blocks, item_tokens: int) -> PackedHost:
         tok_row[s:s + T] = r
         blk[i] = (s, T, r, p0)
         items.extend((i, t0) for t0 in range(0, T, item_tokens))
+    # longest key range first: the attention grid then finishes its long items before the short
+    # ones fill the last wave (an item's result does not depend on its place in the grid)
+    items.sort(key=lambda it_: -(blocks[it_[0]][1] + min(it_[1] + item_tokens, blocks[it_[0]][2])))
     it = np.array(items, dtype=np.int32).reshape(-1, 2)
     max_ctx = max((p0 + T for (_, p0, T) in blocks), default=0)
     return PackedHost(blocks, offsets, tok_pos, tok_row, blk, it, int(max_ctx))
