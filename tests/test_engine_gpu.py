@@ -6,10 +6,12 @@ import pytest
 import torch
 
 from thesis_b200.config import preset
+from thesis_b200.dynamic import B200DynamicSpecEngine
 from thesis_b200.eesd import B200ARBatchEngine, B200SpecEngine
 from thesis_b200.engine import RunConfig
 from thesis_b200.model import ModelWeights
-from thesis_b200.synthetic import synthetic_prompts, synthetic_weights
+from thesis_b200.serving import B200ServingEngine
+from thesis_b200.synthetic import Prompt, synthetic_prompts, synthetic_weights
 
 pytestmark = pytest.mark.gpu
 
@@ -83,3 +85,75 @@ def test_full_size_spec_equals_ar(cuda_dev, name, E, gamma, B, lens):
     sp_e.dm.check()
     assert _outputs(res) == ar
     assert res["metrics"]["spec"]["acceptance_rate"] > 0.2
+
+
+@pytest.mark.parametrize("exits,grange,B,seed", [((1, 3, 5), (2, 8), 3, 0), ((2, 4), (0, 3), 4, 1), ((3,), (1, 1), 2, 2)])
+def test_dynamic_exit_and_draft_length_is_lossless(c1s_bf16, ar_reference, exits, grange, B, seed):
+    """Per-request exit layer and per-request, per-round draft length (coalesced ragged verify):
+    the output equals the AR output bit for bit whatever the draws."""
+    prompts, ref = ar_reference
+    eng = B200DynamicSpecEngine(c1s_bf16, B, 60, MAX_NEW, (2,), ignore_eos=True, exit_layers=exits,
+                                gamma_range=grange, policy_seed=seed)
+    res = eng.run(prompts, RunConfig(mode="static", keep_outputs=True))
+    eng.dm.check()
+    assert _outputs(res) == ref
+    spec = res["metrics"]["spec"]
+    assert sum(spec["exit_hist"].values()) == spec["request_rounds"]
+    if len(exits) > 1:
+        assert sum(1 for v in spec["exit_hist"].values() if v) > 1     # several exits were in play
+    if grange[1] > 0:
+        assert spec["accepted"] > 0
+
+
+def test_dynamic_full_size_llama2_7b_equals_ar(cuda_dev):
+    """BASELINE config 4 shape (Llama2-7B, MHA, exits {4, 8, 12}, draft length 2..8 per request and
+    round, lognormal prompt lengths): speculative tokens equal AR tokens bit for bit."""
+    cfg = preset("llama2-7b")
+    w = ModelWeights.synthetic(cfg, seed=0, dtype=torch.bfloat16, device="cuda", residual_scale_from=4,
+                               residual_scale=0.1)
+    prompts = synthetic_prompts(6, cfg.vocab_size, seed=3, min_len=32, max_len=1536, lengths="lognormal", median=256)
+    rc = RunConfig(mode="static", keep_outputs=True)
+    mp = max(len(p.tokens) for p in prompts)
+    ar_e = B200ARBatchEngine(w, 6, mp, 20, (), ignore_eos=True)
+    ar = _outputs(ar_e.run(prompts, rc))
+    ar_e.free()
+    sp_e = B200DynamicSpecEngine(w, 6, mp, 20, (), ignore_eos=True, exit_layers=(4, 8, 12), gamma_range=(2, 8))
+    res = sp_e.run(prompts, rc)
+    sp_e.dm.check()
+    assert _outputs(res) == ar
+    assert res["metrics"]["spec"]["acceptance_rate"] > 0.1
+
+
+@pytest.mark.parametrize("B,budget,gamma", [(2, 7, 3), (3, 64, 4), (4, 1000, 2)])
+def test_piggyback_prefill_is_lossless(c1s_bf16, ar_reference, B, budget, gamma):
+    """New requests prefilled inside the draft/verify steps (chunks through [0, E) with the drafts,
+    through [E, L) with the verify tokens; a flush through all layers when nothing decodes): the
+    output equals the AR output bit for bit."""
+    prompts, ref = ar_reference
+    eng = B200ServingEngine(c1s_bf16, B, 60, MAX_NEW, (2,), ignore_eos=True, exit_layer=3, gamma=gamma,
+                            piggyback_budget=budget)
+    res = eng.run(prompts, RunConfig(mode="static", keep_outputs=True))
+    eng.dm.check()
+    assert _outputs(res) == ref
+    assert eng.stats["piggyback_tokens"] > 0 and eng.stats["flush_steps"] > 0
+
+
+def test_poisson_driver_with_per_request_lengths(c1s_bf16):
+    """Open-loop Poisson arrivals, per-request output lengths, piggybacked prefill: every measured
+    request completes with its own length and the AR tokens."""
+    base = synthetic_prompts(8, c1s_bf16.cfg.vocab_size, seed=4, min_len=5, max_len=40)
+    rng = np.random.default_rng(0)
+    prompts = [Prompt(p.pid, p.tokens, max_new=int(rng.integers(4, 17))) for p in base]
+    ar_e = B200ARBatchEngine(c1s_bf16, 4, 40, 16, (), ignore_eos=True)
+    ar = _outputs(ar_e.run(base, RunConfig(mode="static", keep_outputs=True)))
+    ar_e.free()
+    eng = B200ServingEngine(c1s_bf16, 3, 40, 16, (), ignore_eos=True, exit_layer=3, gamma=3, piggyback_budget=16)
+    res = eng.run_poisson(prompts, rate_per_s=200.0, n_requests=6, warm_requests=2, seed=0, keep_outputs=True)
+    eng.dm.check()
+    m = res["metrics"]
+    assert m["evaluated_completions"] == 6 and m["ttft_ms_mean"] > 0 and m["wall_throughput_tok_s"] > 0
+    by_pid = {p.pid: p for p in prompts}
+    assert len(res["completions"]) >= 8
+    for c in res["completions"]:
+        want = by_pid[c["pid"]].max_new
+        assert c["generated"] == want and c["tokens"] == ar[c["pid"]][:want]

@@ -35,7 +35,7 @@ def test_packing_metadata():
 def test_registry_contract():
     from thesis_b200 import methods
 
-    assert {"b200_autoregressive", "b200_layerskip"} <= set(methods.METHODS)
+    assert {"b200_autoregressive", "b200_layerskip", "b200_layerskip_dynamic"} <= set(methods.METHODS)
     with pytest.raises(ValueError):
         methods.register(methods.METHODS["b200_layerskip"])
     # the CLI groups coexist with a parser that already has --exit-layer / --gamma (the reference's)
@@ -48,6 +48,10 @@ def test_registry_contract():
     assert a.exit_layer == 8 and a.b200_prefill_chunk == 256
     assert methods.METHODS["b200_layerskip"].tag(a) == "-k8-g4"
     assert methods.METHODS["b200_layerskip"].step_tokens(a) == 5
+    a = ap.parse_args(["--b200-exit-layers", "4,8,12", "--b200-gamma-range", "2,8"])
+    dyn = methods.METHODS["b200_layerskip_dynamic"]
+    assert dyn.step_tokens(a) == 9 and dyn.tag(a) == "-e4_8_12-g2_8"
+    assert dyn.params(a) == {"exit_layers": [4, 8, 12], "gamma_range": [2, 8], "policy_seed": 0}
 
 
 class ToyEngine(DecodeEngine):

@@ -125,3 +125,34 @@ def test_pack_weight_layout(cuda_dev, rows, k):
     wp[:rows] = w
     ref = wp.view(mt, 128, kb, 64).permute(0, 2, 1, 3).reshape(-1)
     assert torch.equal(out, ref)
+
+
+def _one_layer_model(cuda_dev, head_dim, max_seq=1088):
+    from thesis_b200.config import ModelConfig
+    from thesis_b200.model import DeviceModel, ModelWeights
+
+    cfg = ModelConfig(vocab_size=512, dim=8 * head_dim, n_layers=1, n_heads=8, n_kv_heads=2, head_dim=head_dim,
+                      intermediate_size=1024)
+    w = ModelWeights.synthetic(cfg, seed=0, dtype=torch.bfloat16, device=cuda_dev)
+    dm = DeviceModel(w, max_batch=4, max_seq=max_seq, max_tokens=64)
+    g = torch.Generator(device=cuda_dev).manual_seed(1)
+    dm.k_cache.copy_(torch.randn(dm.k_cache.shape, generator=g, device=cuda_dev))   # stands in for a prefill
+    dm.v_cache.copy_(torch.randn(dm.v_cache.shape, generator=g, device=cuda_dev))
+    x = torch.randn(64, cfg.dim, generator=g, device=cuda_dev).bfloat16()
+    return dm, x
+
+
+@pytest.mark.parametrize("pos0", [3, 254, 1000])
+def test_layer_is_batch_invariant_across_step_shapes(cuda_dev, pos0):
+    """A token's layer output does not depend on the call it runs in: token j of a 5-token
+    verify-shaped block equals the same token run alone in a draft-shaped call (4-warp attention
+    variant instead of the 8-warp one, other GEMM token tiles), bit for bit.  This is what makes
+    speculative output identical to autoregressive output."""
+    dm, x = _one_layer_model(cuda_dev, 128)
+    xv = x[:10].clone()
+    dm.forward_layers(xv, dm.upload(dm.pack([(0, pos0, 5), (1, 700, 5)])), 0, 1)
+    for j in range(5):
+        xd = x[j:j + 1].clone()
+        dm.forward_layers(xd, dm.upload(dm.pack([(0, pos0 + j, 1)])), 0, 1)
+        assert torch.equal(xd[0], xv[j]), j
+    dm.check()

@@ -87,12 +87,43 @@ def _b200_spec_build(model, args, batch_size, max_prompt_len, eos):
                           gamma=args.gamma, **_kw(args))
 
 
+def _b200_dyn_args(g) -> None:
+    g.add_argument("--b200-exit-layers", type=str, default="4,8,12",
+                   help="[b200_layerskip_dynamic] exit layers a request may draw (comma-separated)")
+    g.add_argument("--b200-gamma-range", type=str, default="2,8",
+                   help="[b200_layerskip_dynamic] draft length range lo,hi drawn per request and round")
+    g.add_argument("--b200-policy-seed", type=int, default=0, help="[b200_layerskip_dynamic] draw seed")
+    _b200_ar_args(g)
+
+
+def _ints(text: str) -> list:
+    return [int(v) for v in str(text).split(",") if v.strip()]
+
+
+def _b200_dyn_build(model, args, batch_size, max_prompt_len, eos):
+    from .dynamic import B200DynamicSpecEngine
+
+    g = _ints(args.b200_gamma_range)
+    if len(g) != 2:
+        raise SystemExit("--b200-gamma-range takes lo,hi")
+    return B200DynamicSpecEngine(model, batch_size, max_prompt_len, args.max_new_tokens, eos,
+                                 exit_layers=_ints(args.b200_exit_layers), gamma_range=(g[0], g[1]),
+                                 policy_seed=args.b200_policy_seed, **_kw(args))
+
+
 SPECS = [
     MethodSpec("b200_autoregressive", "all N layers per token on the sm_100a packed path (lossless reference)",
                _b200_ar_args, _b200_ar_build),
     MethodSpec("b200_layerskip", "synchronous batched LayerSkip on the sm_100a packed path (fixed E, gamma)",
                _b200_spec_args, _b200_spec_build, tag=lambda a: f"-k{a.exit_layer}-g{a.gamma}", spec_slack=64,
                step_tokens=lambda a: a.gamma + 1, params=lambda a: {"exit_layer": a.exit_layer, "gamma": a.gamma}),
+    MethodSpec("b200_layerskip_dynamic",
+               "LayerSkip with a per-request exit layer and per-request draft length, coalesced ragged verify",
+               _b200_dyn_args, _b200_dyn_build,
+               tag=lambda a: f"-e{a.b200_exit_layers.replace(',', '_')}-g{a.b200_gamma_range.replace(',', '_')}",
+               spec_slack=64, step_tokens=lambda a: _ints(a.b200_gamma_range)[-1] + 1,
+               params=lambda a: {"exit_layers": _ints(a.b200_exit_layers), "gamma_range": _ints(a.b200_gamma_range),
+                                 "policy_seed": a.b200_policy_seed}),
 ]
 
 for _s in SPECS:
