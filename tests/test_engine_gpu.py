@@ -151,9 +151,11 @@ def test_poisson_driver_with_per_request_lengths(c1s_bf16):
     res = eng.run_poisson(prompts, rate_per_s=200.0, n_requests=6, warm_requests=2, seed=0, keep_outputs=True)
     eng.dm.check()
     m = res["metrics"]
-    assert m["evaluated_completions"] == 6 and m["ttft_ms_mean"] > 0 and m["wall_throughput_tok_s"] > 0
-    by_pid = {p.pid: p for p in prompts}
+    # the run ends after n_requests + warm_requests completions; requests assigned before the warm-up
+    # ended are not measured (solutions/engine.py:625-673)
     assert len(res["completions"]) >= 8
+    assert 1 <= m["evaluated_completions"] <= 6 and m["ttft_ms_mean"] > 0 and m["wall_throughput_tok_s"] > 0
+    by_pid = {p.pid: p for p in prompts}
     for c in res["completions"]:
         want = by_pid[c["pid"]].max_new
         assert c["generated"] == want and c["tokens"] == ar[c["pid"]][:want]

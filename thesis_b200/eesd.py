@@ -53,11 +53,11 @@ class _B200Engine(DecodeEngine):
     cols = 1
 
     def __init__(self, model, batch_size, max_prompt_len, max_new_tokens, eos_ids, *, step_tokens: int = 1,
-                 prefill_budget: int = 2048, prefill_chunk: int = 512, **kw):
+                 prefill_budget: int = 2048, prefill_chunk: int = 512, extra_tokens: int = 0, **kw):
         super().__init__(model, batch_size, max_prompt_len, max_new_tokens, eos_ids, **kw)
         self.weights = as_weights(model)
         self.prefill_chunk = prefill_chunk
-        max_tokens = max(self.B * step_tokens, min(prefill_budget, max(prefill_chunk, 1) * self.B))
+        max_tokens = max(self.B * step_tokens + extra_tokens, min(prefill_budget, max(prefill_chunk, 1) * self.B))
         self.dm = DeviceModel(self.weights, self.B, self.max_seq, max_tokens)
         self.device = self.dm.device
         self.cfg = self.weights.cfg

@@ -49,6 +49,7 @@ class SlotState:
     idle: bool = True
     t_assigned: float = 0.0
     decode_ms: float = 0.0
+    max_new: Optional[int] = None   # per-request output budget (None: the engine's max_new_tokens)
 
 
 @dataclass
@@ -130,7 +131,7 @@ class DecodeEngine:
             n += 1
             if not self.ignore_eos and t in self.eos:
                 s.finish_reason = "eos"
-            elif len(s.output) >= self.max_new:
+            elif len(s.output) >= (s.max_new or self.max_new):
                 s.finish_reason = "length"
         if n and self.stop_checker and not self.ignore_eos:
             cut = self.stop_checker(s.output, n)
@@ -158,6 +159,7 @@ class DecodeEngine:
             s.pos, s.last_token = len(prompt.tokens), int(first[slot])
             s.output, s.finish_reason, s.idle = [], None, False
             s.t_assigned, s.decode_ms = now, 0.0
+            s.max_new = min(int(prompt.max_new), self.max_new) if getattr(prompt, "max_new", None) else None
             self._on_assigned(slot)
             self._commit(slot, [first[slot]])
 

@@ -36,6 +36,7 @@ class Prompt:
     pid: str
     tokens: list
     reference: str = ""
+    max_new: Optional[int] = None   # per-request output length (open-loop serving workloads)
 
 
 def layer_shapes(cfg) -> dict:

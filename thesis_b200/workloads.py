@@ -1,0 +1,110 @@
+"""Measurement of the BASELINE configurations beyond the headline one (one JSON line each).
+
+    python -m thesis_b200.workloads c4 [--requests 32] [--new 256]
+    python -m thesis_b200.workloads c5 [--requests 256] [--rate 40] [--budget 256]
+
+c4  Llama2-7B shape (32 layers, dim 4096, 32 heads MHA of 128, SwiGLU 11008, vocab 32000, RoPE
+    theta 10000), bf16, residual outputs of layers >= 4 scaled by 0.1; batch 32, prompt lengths
+    lognormal (median 256, clipped to 32..1536), a per-request exit layer from {4, 8, 12} and a
+    per-request draft length drawn from 2..8 every round (``B200DynamicSpecEngine``), 256 new
+    tokens greedy.  Reports decode throughput next to the autoregressive engine's on the same
+    requests, and whether the two outputs are identical.
+c5  Llama3-8B shape, bf16, residual outputs of layers >= 8 scaled by 0.1; 256 slots, Poisson
+    arrivals at ``--rate`` requests/s, prompt lengths lognormal (median 512, clipped to 64..2048),
+    output lengths uniform in 128..1024, exit layer 8, gamma 4, new-request prefill piggybacked
+    on the draft/verify steps (``B200ServingEngine.run_poisson``).  Reports throughput, TTFT and
+    TPOT of the measured requests.
+
+Weights and prompts are seeded synthetic stand-ins for the checkpoints and datasets the
+reference would use; no dataset item is reproduced.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import time
+
+import numpy as np
+import torch
+
+from .config import preset
+from .engine import RunConfig
+from .model import ModelWeights
+from .synthetic import Prompt, synthetic_prompts
+
+
+def run_c4(args) -> dict:
+    from .dynamic import B200DynamicSpecEngine
+    from .eesd import B200ARBatchEngine
+
+    cfg = preset("llama2-7b")
+    w = ModelWeights.synthetic(cfg, seed=0, dtype=torch.bfloat16, device="cuda", residual_scale_from=4,
+                               residual_scale=0.1)
+    prompts = synthetic_prompts(args.requests, cfg.vocab_size, seed=7, min_len=32, max_len=1536, lengths="lognormal",
+                                median=256)
+    mp = max(len(p.tokens) for p in prompts)
+    rc = RunConfig(mode="static", keep_outputs=True)
+    out = {}
+    for name, make in (("dynamic", lambda: B200DynamicSpecEngine(w, args.requests, mp, args.new, (), ignore_eos=True,
+                                                                 exit_layers=(4, 8, 12), gamma_range=(2, 8))),
+                       ("ar", lambda: B200ARBatchEngine(w, args.requests, mp, args.new, (), ignore_eos=True))):
+        eng = make()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        res = eng.run(prompts, rc)
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+        m = res["metrics"]
+        toks = {c["pid"]: c["tokens"] for c in res["completions"]}
+        out[name] = {"throughput_tok_s": m["throughput_tok_s"], "e2e_tok_s": sum(len(t) for t in toks.values()) / wall,
+                     "steps": m["steps"], "spec": m.get("spec"), "tokens": toks}
+        eng.free()
+        del eng
+        torch.cuda.empty_cache()
+    same = out["dynamic"].pop("tokens") == out["ar"].pop("tokens")
+    return {"workload": "c4", "metric": "generated tokens/s (decode device time), 1 GPU", "unit": "tokens/s",
+            "value": out["dynamic"]["throughput_tok_s"], "ar_value": out["ar"]["throughput_tok_s"],
+            "speedup_vs_ar": out["dynamic"]["throughput_tok_s"] / out["ar"]["throughput_tok_s"],
+            "identical_to_ar": same, "requests": args.requests, "new_tokens": args.new, "detail": out}
+
+
+def run_c5(args) -> dict:
+    from .serving import B200ServingEngine
+
+    cfg = preset("llama3-8b")
+    w = ModelWeights.synthetic(cfg, seed=0, dtype=torch.bfloat16, device="cuda", residual_scale_from=8,
+                               residual_scale=0.1)
+    n_pool = args.requests + args.warm
+    base = synthetic_prompts(n_pool, cfg.vocab_size, seed=9, min_len=64, max_len=2048, lengths="lognormal",
+                             median=512)
+    rng = np.random.default_rng(9)
+    prompts = [Prompt(p.pid, p.tokens, max_new=int(rng.integers(128, 1025))) for p in base]
+    eng = B200ServingEngine(w, args.slots, 2048, 1024, (), ignore_eos=True, exit_layer=8, gamma=4,
+                            piggyback_budget=args.budget)
+    res = eng.run_poisson(prompts, rate_per_s=args.rate, n_requests=args.requests, warm_requests=args.warm, seed=0)
+    eng.dm.check()
+    m = res["metrics"]
+    return {"workload": "c5", "metric": "generated tokens/s (wall clock, open loop), 1 GPU", "unit": "tokens/s",
+            "value": m["wall_throughput_tok_s"], "slots": args.slots, "rate_per_s": args.rate,
+            "requests_measured": m["evaluated_completions"], "metrics": m}
+
+
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("workload", choices=["c4", "c5"])
+    ap.add_argument("--requests", type=int, default=None)
+    ap.add_argument("--new", type=int, default=256)
+    ap.add_argument("--rate", type=float, default=40.0)
+    ap.add_argument("--slots", type=int, default=256)
+    ap.add_argument("--warm", type=int, default=16)
+    ap.add_argument("--budget", type=int, default=256)
+    args = ap.parse_args(argv)
+    if args.requests is None:
+        args.requests = 32 if args.workload == "c4" else 256
+    res = run_c4(args) if args.workload == "c4" else run_c5(args)
+    print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()
