@@ -57,6 +57,7 @@ struct alignas(8) TcParams {
   int tmem_cols;
   int a_packed;     // 1: weight in tile-packed layout (3-D map over 16 KB tiles), 0: row-major 2-D map
   int acc_cols;     // TMEM columns of the accumulator (bn, or 2 bn for SwiGLU)
+  int res_stage;    // split-K RESIDUAL: the owned slice's residual rows arrive by bulk copies (256 B each)
   const bf16* residual;
   int ld_res;
   bf16* y;
@@ -127,7 +128,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* full = bars;
   uint64_t* empty = bars + p.stages;
   uint64_t* accb = bars + 2 * p.stages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accb + 1);
+  uint64_t* epib = accb + 1;                 // split-K: staged partials / residual landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accb + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -143,6 +145,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(smem_u32(&empty[s]), 1);
     }
     mbar_init(smem_u32(accb), 1);
+    mbar_init(smem_u32(epib), 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -258,6 +261,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const bool row_ok = row < p.n_out;
   const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16);
   bool ok = true;
+  bool copies_issued = false;   // split-K staging: this thread issued bulk copies into epib
   if (epi_warp) {
     pdl_wait();
     ok = mbar_wait(smem_u32(accb), 0, abort_flag);
@@ -314,13 +318,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     // it does not own (laid out [column / 4][128 rows] float4: a warp's 32 rows are 512 contiguous
     // bytes), one cluster barrier (release / acquire at cluster scope) publishes them, then every
     // owner adds the splits in split order - its own straight from TMEM - and runs the epilogue.
+    // The other splits' partials of the owned slice (one contiguous run per split) and, for the
+    // residual epilogue, the slice's residual rows are brought into the idle stage memory by bulk
+    // copies, so the owner phase waits for one round trip instead of one per 16-column chunk.
     // The cluster's CTAs are co-scheduled, so the barrier never waits on an unscheduled CTA.
     const int S = p.splits;
     const int rank = (int)cluster_rank();
     const int slice = ((p.bn + S - 1) / S + 15) / 16 * 16;
-    const int own_lo = rank * slice, own_hi = min(p.bn, own_lo + slice);
+    const int own_lo = min(p.bn, rank * slice), own_hi = min(p.bn, own_lo + slice);
+    const int own_w = own_hi - own_lo;                 // multiple of 16
     const size_t part_f4 = (size_t)p.acc_cols * 32;   // float4s in one split's partial tile
     float4* tile_parts = p.partials + (size_t)((out_tile * gridDim.x + tok_tile) * S) * part_f4;
+    const uint32_t run_bytes = (uint32_t)own_w * 512u;              // one split, one accumulator
+    const uint32_t part_stage = (uint32_t)(S - 1) * kNA * run_bytes;
+    const int res_tokens = EPI == EESD_EPI_RESIDUAL && p.res_stage ? max(0, min(own_w, p.n_tok - (n0 + own_lo))) : 0;
+    const uint32_t res_bytes = (uint32_t)res_tokens * 256u;
+    const bool staged = own_w > 0 && part_stage + res_bytes <= (uint32_t)p.stages * stage_bytes;
+    const uint32_t stage0 = smem_u32(smem);
     if (epi_warp && ok) {
       float4* mine = tile_parts + (size_t)rank * part_f4;
       for (int c = half * 16; c < p.bn; c += 32) {
@@ -335,9 +349,91 @@ __global__ void __launch_bounds__(kThreads, 1)
             mine[(size_t)(g0 + j) * 128 + row_local] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
         }
       }
+      fence_proxy_async_global();   // the peers read these stores with bulk (async-proxy) copies
+    }
+    bool issuer_ok = true;
+    if (staged && warp == 0 && lane == 0) {
+      // the stage memory is free once every MMA has completed
+      issuer_ok = mbar_wait(smem_u32(accb), 0, abort_flag);
+      if (issuer_ok) {
+        copies_issued = true;
+        mbar_arrive_expect_tx(smem_u32(epib), part_stage + res_bytes);
+        for (int t = 0; t < res_tokens; ++t)
+          bulk_g2s(stage0 + part_stage + (uint32_t)t * 256u, p.residual + (size_t)(n0 + own_lo + t) * p.ld_res + m0,
+                   256u, smem_u32(epib));
+      } else {
+        set_status(p.status, kStatusTimeoutEpilogue);
+        *abort_flag = 1;
+      }
     }
     cluster_sync();
-    if (epi_warp && ok) {
+    if (staged && warp == 0 && lane == 0 && issuer_ok) {
+      fence_proxy_async_global();
+      uint32_t dst = stage0;
+      for (int sp = 0; sp < S; ++sp) {
+        if (sp == rank) continue;
+        const float4* src = tile_parts + (size_t)sp * part_f4;
+#pragma unroll
+        for (int part = 0; part < kNA; ++part, dst += run_bytes)
+          bulk_g2s(dst, src + (size_t)((part * p.bn + own_lo) / 4) * 128, run_bytes, smem_u32(epib));
+      }
+    }
+    if (epi_warp && ok && staged) {
+      if (!mbar_wait(smem_u32(epib), 0, abort_flag)) {
+        set_status(p.status, kStatusTimeoutEpilogue);
+        *abort_flag = 1;
+      } else {
+        const float4* st4 = reinterpret_cast<const float4*>(smem);
+        const bf16* res_s = reinterpret_cast<const bf16*>(smem + part_stage);
+        for (int c = own_lo + half * 16; c < own_hi; c += 32) {
+          float g[16], u[16];
+#pragma unroll 1
+          for (int sp = 0, k = 0; sp < S; ++sp) {
+            float pg[16], pu[16];
+            if (sp == rank) {
+              tmem_ld16(lane_base + c, pg);
+              if (kNA == 2) tmem_ld16(lane_base + p.bn + c, pu);
+            } else {
+              // staged run k of this split: [accumulator][own_w / 4][128] float4
+              const float4* src = st4 + (size_t)k * kNA * (own_w / 4) * 128;
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const float4 a = src[(size_t)((c - own_lo) / 4 + j) * 128 + row_local];
+                pg[4 * j] = a.x;
+                pg[4 * j + 1] = a.y;
+                pg[4 * j + 2] = a.z;
+                pg[4 * j + 3] = a.w;
+                if (kNA == 2) {
+                  const float4 b4 = src[(size_t)(own_w / 4 + (c - own_lo) / 4 + j) * 128 + row_local];
+                  pu[4 * j] = b4.x;
+                  pu[4 * j + 1] = b4.y;
+                  pu[4 * j + 2] = b4.z;
+                  pu[4 * j + 3] = b4.w;
+                }
+              }
+              ++k;
+            }
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              g[j] = sp == 0 ? pg[j] : g[j] + pg[j];
+              if (kNA == 2) u[j] = sp == 0 ? pu[j] : u[j] + pu[j];
+            }
+          }
+          if (row_ok) {
+            float r[16];
+            if (EPI == EESD_EPI_RESIDUAL) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const int tl = c - own_lo + j;
+                r[j] = tl < res_tokens ? __bfloat162float(res_s[tl * 128 + row_local]) : 0.f;
+              }
+              if (!p.res_stage) load_residual<EPI, 16>(p, n0 + c, row, r);
+            }
+            epilogue_cols_r<EPI, 16>(p, n0 + c, row, g, u, r);
+          }
+        }
+      }
+    } else if (epi_warp && ok) {
       for (int c = half * 16; c < p.bn; c += 32) {
         if (c < own_lo || c >= own_hi) continue;
         float g[16], u[16];
@@ -375,6 +471,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (row_ok) epilogue_cols<EPI, 16>(p, n0 + c, row, g, u);
       }
+    }
+  }
+  if (copies_issued && *abort_flag) {
+    // the bulk copies this CTA issued land before it exits, even if its epilogue gave up
+    for (uint32_t i = 0; i < kSpinLimit && !mbar_try_wait(smem_u32(epib), 0); ++i) {
     }
   }
   tc_fence_before();
@@ -587,6 +688,9 @@ int tc_gemm_launch(int epi, const CUtensorMap& map_w, const void* x, int n_tok, 
   p.tmem_cols = pl.tmem_cols;
   p.a_packed = a_packed;
   p.acc_cols = pl.acc_cols;
+  // residual rows of an owned slice by 256-byte bulk copies: whole 128-row tiles, 16-byte aligned rows
+  p.res_stage = epi == EESD_EPI_RESIDUAL && n_out % kBM == 0 && ld_res % 8 == 0 &&
+                (reinterpret_cast<uintptr_t>(residual) & 15) == 0;
   p.partials = static_cast<float4*>(scratch.partials);
   p.residual = static_cast<const bf16*>(residual);
   p.ld_res = ld_res;
