@@ -184,10 +184,13 @@ int eesd_gemm(int dtype, int epilogue, const void* x, const void* w, const void*
  * tile, else a fixed multiple of 16 up to 256); numerics-neutral by design.  EESD_OPT_SPLITS:
  * split-K count (0 = derived from the weight shape; any fixed value keeps batch invariance but
  * changes the summation order, so AR and speculative runs must use the same value).
- * EESD_OPT_STAGES: TMA pipeline depth (0 = as many stages as fit; numerics-neutral). */
+ * EESD_OPT_STAGES: TMA pipeline depth (0 = as many stages as fit; numerics-neutral).
+ * EESD_OPT_PAIR: 1 (default) runs SwiGLU GEMMs on CTA pairs (cta_group::2, M = 256) where the
+ * weight shape allows, 0 on single CTAs; AR and speculative runs must use the same value. */
 #define EESD_OPT_MMA_N 1
 #define EESD_OPT_SPLITS 2
 #define EESD_OPT_STAGES 3
+#define EESD_OPT_PAIR 4
 int eesd_set_option(int option, int value);
 
 /* Exit head that allocates nothing, for callers that cannot call cudaMalloc (a serving

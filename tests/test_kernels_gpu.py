@@ -77,6 +77,31 @@ def test_gemm_bf16_is_batch_invariant(cuda_dev, mma_n):
         lib.call("eesd_set_option", lib.OPT_MMA_N, 0)
 
 
+def test_gemm_swiglu_on_cta_pairs(cuda_dev):
+    """W13 + SwiGLU at the 8B shape runs on CTA pairs (cta_group::2, M = 256, each CTA loading half
+    of the token tile): it matches the fp32 reference and the single-CTA kernel, and a token row's
+    result is bit-identical whatever the number of tokens in the launch."""
+    g = torch.Generator(device=cuda_dev).manual_seed(11)
+    k, inter = 4096, 14336
+    x = torch.randn(333, k, device=cuda_dev, generator=g).bfloat16()
+    w13 = (torch.randn(2 * inter, k, device=cuda_dev, generator=g) * 0.02).bfloat16()
+
+    def swiglu(xx):
+        return _gemm(xx, w13, lib.EPI_SWIGLU, n_out=inter, up_offset=inter)
+
+    full = swiglu(x)
+    gu = (x.float() @ w13.float().T).bfloat16().float()
+    ref = (torch.nn.functional.silu(gu[:, :inter]).bfloat16().float() * gu[:, inter:]).bfloat16()
+    _close(full, ref, 1e-2)
+    for n in (1, 16, 64, 160, 320):
+        assert torch.equal(swiglu(x[:n].contiguous()), full[:n]), n
+    lib.call("eesd_set_option", lib.OPT_PAIR, 0)
+    try:
+        _close(swiglu(x), ref, 1e-2)
+    finally:
+        lib.call("eesd_set_option", lib.OPT_PAIR, 1)
+
+
 @pytest.mark.parametrize("n_tok", [1, 70, 300])
 def test_gemm_f32(cuda_dev, n_tok):
     g = torch.Generator(device=cuda_dev).manual_seed(1)

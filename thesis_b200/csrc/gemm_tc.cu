@@ -116,13 +116,20 @@ __device__ __forceinline__ void epilogue_cols(const TcParams& p, int t0, int row
   epilogue_cols_r<EPI, NC>(p, t0, row, g, u, r);
 }
 
-template <int EPI>
+// PAIR: a (2,1,1) cluster of two CTAs computes one 256-row x bn tile with cta_group::2 MMAs.  CTA r
+// holds weight row tile 2 * blockIdx.z + r (its 128 accumulator lanes) and token rows
+// [n0 + r bn/2, n0 + (r + 1) bn/2) of the tile; both CTAs' tile loads complete on the even CTA's
+// `full` barriers, the even CTA alone issues the MMAs, and it commits to the `empty` and
+// accumulator barriers of both CTAs (one commit per CTA).  Per SM, a k-block moves 128 weight rows and bn/2 token rows
+// for 128 x bn outputs, where a single CTA moves 128 + bn rows.
+template <int EPI, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x, TcParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   constexpr int kNA = (EPI == EESD_EPI_SWIGLU) ? 2 : 1;
-  const uint32_t b_bytes = (uint32_t)p.bn * kBK * 2;
+  const int b_rows = PAIR ? p.bn / 2 : p.bn;     // token rows this CTA loads per k-block
+  const uint32_t b_bytes = (uint32_t)b_rows * kBK * 2;
   const uint32_t stage_bytes = kNA * kATileBytes + b_bytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)p.stages * stage_bytes);
   uint64_t* full = bars;
@@ -133,7 +140,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tok_tile = blockIdx.x, out_tile = blockIdx.y, split = blockIdx.z;
+  const int rank = PAIR ? (int)cluster_rank() : 0;          // CTA of the pair (0 issues the MMAs)
+  const int tok_tile = PAIR ? blockIdx.y : blockIdx.x;
+  const int out_tile = PAIR ? 2 * blockIdx.z + rank : blockIdx.y;
+  const int split = PAIR ? 0 : blockIdx.z;
   const int n0 = tok_tile * p.bn, m0 = out_tile * kBM;
   const int kb_begin = split * p.kb_per;
   const int nkb = min(p.kb_total, kb_begin + p.kb_per) - kb_begin;
@@ -154,11 +164,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&map_x);
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), (uint32_t)p.tmem_cols);
-    tmem_relinquish();
+    if (PAIR) {
+      tmem_alloc_pair(smem_u32(tmem_slot), (uint32_t)p.tmem_cols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(smem_u32(tmem_slot), (uint32_t)p.tmem_cols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  // the pair's barriers and TMEM exist before either CTA signals the other
+  if (PAIR) cluster_sync();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -166,12 +183,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       // Weight tiles do not depend on the previous kernel: the first stages' weight loads are issued
       // before waiting for it (programmatic dependent launch), the activation loads after.
+      // fb: the `full` barrier that counts the load (PAIR: the even CTA's, as a cluster address)
       auto load_a = [&](int i, uint32_t st, uint32_t fb) {
         const int kb = kb_begin + i;
         if (p.a_packed) {
           // tile (row tile, k-block) = one contiguous 16 KB block: tiles of a row tile are consecutive
-          tma_load_3d(st, &map_w, 0, 0, out_tile * p.kb_total + kb, fb);
-          if (kNA == 2) tma_load_3d(st + kATileBytes, &map_w, 0, 0, (out_tile + p.up_offset / kBM) * p.kb_total + kb, fb);
+          const int z0 = out_tile * p.kb_total + kb, z1 = (out_tile + p.up_offset / kBM) * p.kb_total + kb;
+          if (PAIR) {
+            tma_load_3d_pair(st, &map_w, 0, 0, z0, fb);
+            if (kNA == 2) tma_load_3d_pair(st + kATileBytes, &map_w, 0, 0, z1, fb);
+          } else {
+            tma_load_3d(st, &map_w, 0, 0, z0, fb);
+            if (kNA == 2) tma_load_3d(st + kATileBytes, &map_w, 0, 0, z1, fb);
+          }
+        } else if (PAIR) {
+          tma_load_2d_pair(st, &map_w, kb * kBK, m0, fb);
+          if (kNA == 2) tma_load_2d_pair(st + kATileBytes, &map_w, kb * kBK, p.up_offset + m0, fb);
         } else {
           tma_load_2d(st, &map_w, kb * kBK, m0, fb);
           if (kNA == 2) tma_load_2d(st + kATileBytes, &map_w, kb * kBK, p.up_offset + m0, fb);
@@ -180,19 +207,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto load_b = [&](int i, uint32_t st, uint32_t fb) {
         const int kx = (kb_begin + i) * kBK;
         const uint32_t bst = st + kNA * kATileBytes;
-        tma_load_2d(bst, &map_x, kx, n0, fb);
-        if (p.b_boxes == 2) tma_load_2d(bst + (uint32_t)(p.bn / 2) * 128u, &map_x, kx, n0 + p.bn / 2, fb);
+        if (PAIR) {
+          tma_load_2d_pair(bst, &map_x, kx, n0 + rank * b_rows, fb);
+        } else {
+          tma_load_2d(bst, &map_x, kx, n0, fb);
+          if (p.b_boxes == 2) tma_load_2d(bst + (uint32_t)(p.bn / 2) * 128u, &map_x, kx, n0 + p.bn / 2, fb);
+        }
+      };
+      // the even CTA of a pair expects both CTAs' bytes on its barrier; the odd CTA only loads
+      const bool expects = !PAIR || rank == 0;
+      const uint32_t tx_bytes = PAIR ? 2u * stage_bytes : stage_bytes;
+      auto fbar = [&](int slot) {
+        const uint32_t local = smem_u32(&full[slot]);
+        return PAIR ? dsmem_addr(local, 0) : local;
       };
       const int pre = min(p.stages, nkb);
       for (int i = 0; i < pre; ++i) {
-        const uint32_t fb = smem_u32(&full[i]);
-        mbar_arrive_expect_tx(fb, stage_bytes);
-        load_a(i, smem_u32(smem + (size_t)i * stage_bytes), fb);
+        if (expects) mbar_arrive_expect_tx(smem_u32(&full[i]), tx_bytes);
+        load_a(i, smem_u32(smem + (size_t)i * stage_bytes), fbar(i));
       }
       pdl_wait();
-      for (int i = 0; i < pre; ++i) load_b(i, smem_u32(smem + (size_t)i * stage_bytes), smem_u32(&full[i]));
+      for (int i = 0; i < pre; ++i) load_b(i, smem_u32(smem + (size_t)i * stage_bytes), fbar(i));
       const int stages = p.stages;
-      const uint32_t smem0 = smem_u32(smem), full0 = smem_u32(full), empty0 = smem_u32(empty);
+      const uint32_t smem0 = smem_u32(smem), empty0 = smem_u32(empty);
       int s = pre % stages, ph = (pre / stages) & 1;   // ring slot of k-block i and its fill parity
       for (int i = pre; i < nkb; ++i) {
         // slot s was last filled for k-block i - stages: wait for the MMAs that read it
@@ -201,9 +238,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           *abort_flag = 1;
           break;
         }
-        const uint32_t fb = full0 + 8u * s;
-        mbar_arrive_expect_tx(fb, stage_bytes);
+        if (expects) mbar_arrive_expect_tx(smem_u32(&full[s]), tx_bytes);
         const uint32_t st = smem0 + (uint32_t)s * stage_bytes;
+        const uint32_t fb = fbar(s);
         load_a(i, st, fb);
         load_b(i, st, fb);
         if (++s == stages) { s = 0; ph ^= 1; }
@@ -211,11 +248,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else if (warp == 1) {
-    if (lane == 0) {
+    if (lane == 0 && (!PAIR || rank == 0)) {
       // This single-thread loop is on the critical path (one tcgen05.mma per 4 KB of weights at
       // small token counts): loop-invariant values live in registers, descriptors are built once
       // per stage and stepped by adding to their 14-bit start-address field (bytes / 16).
-      const uint32_t idesc = idesc_bf16_f32(kBM, p.mma_n);
+      const uint32_t idesc = idesc_bf16_f32(PAIR ? 2 * kBM : kBM, p.mma_n);
       const int stages = p.stages, bn = p.bn, mma_n = p.mma_n;
       const uint32_t full0 = smem_u32(full), empty0 = smem_u32(empty);
       const uint64_t desc_hi = sw128_kmajor_desc(0);
@@ -238,15 +275,32 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
           const uint64_t a_k = da + 2u * kk;            // +32 bytes along K
           uint64_t b_k = db + 2u * kk;
-          for (int nb = 0; nb < bn; nb += mma_n, b_k += sub_lo) {
-            tc_mma_f16(tmem_base + nb, a_k, b_k, idesc, acc);
-            if (kNA == 2) tc_mma_f16(tmem_base + bn + nb, a_k + (kATileBytes >> 4), b_k, idesc, acc);
+          if (PAIR) {   // one MMA per accumulator spans the whole token tile (mma_n == bn <= 256)
+            tc_mma_f16_pair(tmem_base, a_k, b_k, idesc, acc);
+            if (kNA == 2) tc_mma_f16_pair(tmem_base + bn, a_k + (kATileBytes >> 4), b_k, idesc, acc);
+          } else {
+            for (int nb = 0; nb < bn; nb += mma_n, b_k += sub_lo) {
+              tc_mma_f16(tmem_base + nb, a_k, b_k, idesc, acc);
+              if (kNA == 2) tc_mma_f16(tmem_base + bn + nb, a_k + (kATileBytes >> 4), b_k, idesc, acc);
+            }
           }
         }
-        tc_commit(empty0 + 8u * s);
+        if (PAIR) {   // the stage is free in both CTAs
+          tc_commit_pair(empty0 + 8u * s);
+          tc_commit_pair(dsmem_addr(empty0 + 8u * s, 1));
+        } else {
+          tc_commit(empty0 + 8u * s);
+        }
         if (++s == stages) { s = 0; ph ^= 1; }
       }
-      if (ok) tc_commit(smem_u32(accb));
+      if (ok) {
+        if (PAIR) {
+          tc_commit_pair(smem_u32(accb));
+          tc_commit_pair(dsmem_addr(smem_u32(accb), 1));
+        } else {
+          tc_commit(smem_u32(accb));
+        }
+      }
     }
     __syncwarp();
   }
@@ -481,9 +535,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncwarp();
   __syncthreads();
+  // a CTA of a pair leaves only when both are done: the even CTA's MMAs and commits reach the odd
+  // CTA's TMEM and barriers, the odd CTA's loads reach the even CTA's barriers
+  if (PAIR) cluster_sync();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, (uint32_t)p.tmem_cols);
+    if (PAIR)
+      tmem_dealloc_pair(tmem_base, (uint32_t)p.tmem_cols);
+    else
+      tmem_dealloc(tmem_base, (uint32_t)p.tmem_cols);
   }
 }
 
@@ -493,6 +553,7 @@ std::once_flag g_encode_once;
 int g_mma_n_option = 0;   // 0: one MMA spans the whole token tile
 int g_splits_option = 0;  // 0: split count from the weight shape
 int g_stages_option = 0;  // 0: as many stages as the shared-memory budget holds
+int g_pair_option = 1;    // 1: SwiGLU GEMMs whose row tiles pair up run on CTA pairs (cta_group::2)
 
 int next_pow2(int v) {
   int p = 32;
@@ -500,11 +561,11 @@ int next_pow2(int v) {
   return p;
 }
 
-template <int EPI>
+template <int EPI, bool PAIR>
 int ensure_smem_attr(size_t bytes) {
   static size_t set = 0;
   if (bytes > set) {
-    if (cudaFuncSetAttribute(tc_gemm_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) !=
+    if (cudaFuncSetAttribute(tc_gemm_kernel<EPI, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) !=
         cudaSuccess)
       return EESD_ERR_CUDA;
     set = bytes;
@@ -515,7 +576,29 @@ int ensure_smem_attr(size_t bytes) {
 template <int EPI>
 int launch(const TcPlan& pl, const CUtensorMap& map_w, const CUtensorMap& map_x, const TcParams& p,
            cudaStream_t stream) {
-  int rc = ensure_smem_attr<EPI>(pl.smem);
+  if constexpr (EPI == EESD_EPI_SWIGLU) {
+    if (pl.pair) {   // CTA pairs: grid (pair member, token tile, 256-row tile), clusters of 2
+      int rc = ensure_smem_attr<EPI, true>(pl.smem);
+      if (rc) return rc;
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(2, pl.tok_tiles, pl.out_tiles / 2);
+      cfg.blockDim = dim3(kThreads);
+      cfg.dynamicSmemBytes = pl.smem;
+      cfg.stream = stream;
+      cudaLaunchAttribute attr[2];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[1].val.programmaticStreamSerializationAllowed = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 2;
+      return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<EPI, true>, map_w, map_x, p) == cudaSuccess ? EESD_OK
+                                                                                               : EESD_ERR_CUDA;
+    }
+  }
+  int rc = ensure_smem_attr<EPI, false>(pl.smem);
   if (rc) return rc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(pl.tok_tiles, pl.out_tiles, pl.splits);
@@ -531,7 +614,7 @@ int launch(const TcPlan& pl, const CUtensorMap& map_w, const CUtensorMap& map_x,
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<EPI>, map_w, map_x, p) == cudaSuccess ? EESD_OK : EESD_ERR_CUDA;
+  return cudaLaunchKernelEx(&cfg, tc_gemm_kernel<EPI, false>, map_w, map_x, p) == cudaSuccess ? EESD_OK : EESD_ERR_CUDA;
 }
 
 }  // namespace
@@ -607,6 +690,7 @@ int pack_weight(const void* w, int rows, int k, void* out, cudaStream_t s) {
 void tc_set_mma_n(int n) { g_mma_n_option = n; }
 void tc_set_splits(int n) { g_splits_option = n; }
 void tc_set_stages(int n) { g_stages_option = n; }
+void tc_set_pair(int n) { g_pair_option = n; }
 
 TcPlan tc_plan(int n_tok, int n_out, int k, int epi) {
   TcPlan pl{};
@@ -643,7 +727,12 @@ TcPlan tc_plan(int n_tok, int n_out, int k, int epi) {
   pl.kb_per = (pl.kb_total + s - 1) / s;
   pl.splits = (pl.kb_total + pl.kb_per - 1) / pl.kb_per;
   const int na = epi == EESD_EPI_SWIGLU ? 2 : 1;
-  const size_t stage = (size_t)na * kATileBytes + (size_t)pl.bn * kBK * 2;
+  // CTA pairs for unsplit SwiGLU tiles (a whole number of 256-row tiles, one MMA per accumulator);
+  // the choice depends on the weight shape and the option only, never on n_tok
+  pl.pair = epi == EESD_EPI_SWIGLU && g_pair_option && mma_fixed == 0 && pl.splits == 1 && n_out % (2 * kBM) == 0 &&
+            pl.bn <= 256;
+  if (pl.pair) pl.mma_n = pl.bn;
+  const size_t stage = (size_t)na * kATileBytes + (size_t)(pl.pair ? pl.bn / 2 : pl.bn) * kBK * 2;
   pl.stages = (int)std::min<size_t>(8, kSmemBudget / stage);
   if (g_stages_option >= 2 && (size_t)g_stages_option * stage <= kSmemBudget) pl.stages = g_stages_option;
   pl.smem = (size_t)pl.stages * stage + 1024 + 256;
@@ -671,7 +760,7 @@ int tc_gemm_launch(int epi, const CUtensorMap& map_w, const void* x, int n_tok, 
                            (reinterpret_cast<uintptr_t>(scratch.partials) & 15)))
     return EESD_ERR_ARG;
   CUtensorMap map_x;
-  int rc = encode_kmajor_map(&map_x, x, n_tok, k, pl.b_boxes == 2 ? pl.bn / 2 : pl.bn);
+  int rc = encode_kmajor_map(&map_x, x, n_tok, k, (pl.b_boxes == 2 || pl.pair) ? pl.bn / 2 : pl.bn);
   if (rc) return rc;
   TcParams p{};
   p.n_tok = n_tok;

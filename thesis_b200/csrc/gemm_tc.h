@@ -15,6 +15,7 @@ typedef CUresult (*PFN_encodeTiled_t)(CUtensorMap*, CUtensorMapDataType, cuuint3
 
 struct TcPlan {
   int tok_tiles, out_tiles, bn, b_boxes, mma_n, kb_total, kb_per, splits, stages, acc_cols, tmem_cols;
+  int pair;               // 1: CTA pairs (cta_group::2), grid (2, tok_tiles, out_tiles / 2)
   size_t smem;
   size_t partial_bytes;   // split-K scratch the launch needs (0 without split)
 };
@@ -32,6 +33,7 @@ TcPlan tc_plan(int n_tok, int n_out, int k, int epi);
 void tc_set_mma_n(int n);
 void tc_set_splits(int n);
 void tc_set_stages(int n);
+void tc_set_pair(int n);
 // a_packed = 1: map_w is a tile-packed weight map (encode_packed_map), else a row-major 2-D map
 int tc_gemm_launch(int epi, const CUtensorMap& map_w, const void* x, int n_tok, int n_out, int k, int up_offset,
                    const void* residual, int ld_res, void* y, int ld_y, unsigned long long* keys, int* status,

@@ -579,6 +579,11 @@ int eesd_set_option(int option, int value) {
     tc_set_stages(value);
     return EESD_OK;
   }
+  if (option == 4) {   // tcgen05 CTA pairs for SwiGLU GEMMs: 1 = on (default), 0 = off (numerics-neutral)
+    if (value < 0 || value > 1) return fail(EESD_ERR_ARG, "pair %d", value);
+    tc_set_pair(value);
+    return EESD_OK;
+  }
   return fail(EESD_ERR_ARG, "unknown option %d", option);
 }
 
