@@ -167,6 +167,21 @@ int eesd_scatter_ids(const int32_t* ids, const int32_t* idx, int32_t* table, int
 int eesd_greedy_accept(const int32_t* y, const int32_t* vinfo, int nv, int32_t* seq_buf, int stride, int32_t* acc,
                        void* stream);
 
+/* Device-built metadata of one synchronous draft/verify round (gamma drafts + 1 verify), so the
+ * host can enqueue round r+1 before it reads round r's acceptance (the reference's host packing,
+ * solutions/packed.py:81-139, and position update, solutions/engine.py:373-396, done on the GPU).
+ * act [n]: the round's cache rows; pos [max_batch]: round-start position per row.  out holds
+ * eesd_round_meta_ints(n, gamma, item_tokens) int32, cols = gamma + 1, ni = ceil(cols/item_tokens):
+ *   shallow step j = 0..cols-1 at j * 10 n: tok_pos [n] = pos + j, tok_row [n], blk [n, 4] =
+ *     (i, 1, row, pos + j), items [n, 2] = (i, 0), src [n] = row * cols + j, dst [n] = src + 1
+ *   verify at cols * 10 n: tok_pos [n cols], tok_row [n cols], blk [n, 4] = (i cols, cols, row,
+ *     pos), items [n ni, 2], rows [n cols] = row * cols + t, vinfo [n, 3] = (i cols, cols, row)
+ * eesd_round_advance: pos[act[i]] += acc[i] + 1 (rollback by length, solutions/engine.py:12-14). */
+size_t eesd_round_meta_ints(int n, int gamma, int item_tokens);
+int eesd_round_meta(const int32_t* act, int n, const int32_t* pos, int max_batch, int gamma, int item_tokens,
+                    int32_t* out, void* stream);
+int eesd_round_advance(const int32_t* act, int n, const int32_t* acc, int32_t* pos, int max_batch, void* stream);
+
 /* ------------------------------------------------------------------------------------ */
 /* Primitive kernels (exported for tests and for callers composing their own step).    */
 

@@ -665,6 +665,67 @@ __global__ void greedy_accept_kernel(const int32_t* __restrict__ y, const int32_
   sb[0] = y[start + a];
 }
 
+// Packed metadata of one draft/verify round, built on the device from the round-start positions
+// (the host does not wait for the previous round's acceptance).  Thread (i, t): request i of the
+// active list, token t of its round; layout in round_meta_ints().
+__global__ void round_meta_kernel(const int32_t* __restrict__ act, int n, const int32_t* __restrict__ pos,
+                                  int max_batch, int cols, int item_tokens, int32_t* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= n * cols) return;
+  const int i = idx / cols, t = idx - i * cols;
+  const int slot = act[i];
+  const int p0 = (slot >= 0 && slot < max_batch) ? pos[slot] : 0;
+  // shallow step t: token t of every request, one token per block
+  int32_t* st = out + (size_t)t * 10 * n;
+  st[i] = p0 + t;                                   // tok_pos
+  st[n + i] = slot;                                 // tok_row
+  st[2 * n + 4 * i] = i;                            // blk (start, T, row, pos0)
+  st[2 * n + 4 * i + 1] = 1;
+  st[2 * n + 4 * i + 2] = slot;
+  st[2 * n + 4 * i + 3] = p0 + t;
+  st[6 * n + 2 * i] = i;                            // items (block, first token)
+  st[6 * n + 2 * i + 1] = 0;
+  st[8 * n + i] = slot * cols + t;                  // seq_buf / exit_h row of the token
+  st[9 * n + i] = slot * cols + t + 1;              // seq_buf cell of its draft
+  // verify step: all cols tokens of every request
+  const int ni = (cols + item_tokens - 1) / item_tokens;
+  int32_t* v = out + (size_t)cols * 10 * n;
+  const int nt = n * cols;
+  v[i * cols + t] = p0 + t;                         // tok_pos
+  v[nt + i * cols + t] = slot;                      // tok_row
+  int32_t* vblk = v + 2 * nt;
+  int32_t* vitems = vblk + 4 * n;
+  int32_t* vrows = vitems + 2 * n * ni;
+  int32_t* vinfo = vrows + nt;
+  vrows[i * cols + t] = slot * cols + t;
+  if (t == 0) {
+    vblk[4 * i] = i * cols;
+    vblk[4 * i + 1] = cols;
+    vblk[4 * i + 2] = slot;
+    vblk[4 * i + 3] = p0;
+    for (int k = 0; k < ni; ++k) {
+      vitems[2 * (i * ni + k)] = i;
+      vitems[2 * (i * ni + k) + 1] = k * item_tokens;
+    }
+    vinfo[3 * i] = i * cols;
+    vinfo[3 * i + 1] = cols;
+    vinfo[3 * i + 2] = slot;
+  }
+}
+
+// Round-start positions of the next round: every request advances by its accepted drafts + 1.
+__global__ void round_advance_kernel(const int32_t* __restrict__ act, int n, const int32_t* __restrict__ acc,
+                                     int32_t* __restrict__ pos, int max_batch) {
+  pdl_trigger();
+  pdl_wait();
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int slot = act[i];
+  if (slot >= 0 && slot < max_batch) pos[slot] += acc[i] + 1;
+}
+
 __global__ void keys_to_ids_kernel(const unsigned long long* __restrict__ keys, int32_t* __restrict__ ids, int n) {
   pdl_trigger();
   pdl_wait();
@@ -886,6 +947,18 @@ int launch_greedy_accept(const int32_t* y, const int32_t* vinfo, int nv, int32_t
                          cudaStream_t s) {
   if (nv <= 0) return EESD_OK;
   launch_pdl(greedy_accept_kernel, dim3((nv + 127) / 128), dim3(128), 0, s, y, vinfo, nv, seq_buf, stride, acc);
+  return launched();
+}
+int launch_round_meta(const int32_t* act, int n, const int32_t* pos, int max_batch, int cols, int item_tokens,
+                      int32_t* out, cudaStream_t s) {
+  if (n <= 0) return EESD_OK;
+  launch_pdl(round_meta_kernel, dim3((n * cols + 127) / 128), dim3(128), 0, s, act, n, pos, max_batch, cols,
+             item_tokens, out);
+  return launched();
+}
+int launch_round_advance(const int32_t* act, int n, const int32_t* acc, int32_t* pos, int max_batch, cudaStream_t s) {
+  if (n <= 0) return EESD_OK;
+  launch_pdl(round_advance_kernel, dim3((n + 127) / 128), dim3(128), 0, s, act, n, acc, pos, max_batch);
   return launched();
 }
 int launch_keys_to_ids(const unsigned long long* keys, int32_t* ids, int n, cudaStream_t s) {

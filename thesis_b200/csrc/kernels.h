@@ -48,6 +48,9 @@ int launch_gather_ids(const int32_t* table, const int32_t* idx, int32_t* ids, in
 int launch_scatter_ids(const int32_t* ids, const int32_t* idx, int32_t* table, int n, cudaStream_t s);
 int launch_greedy_accept(const int32_t* y, const int32_t* vinfo, int nv, int32_t* seq_buf, int stride, int32_t* acc,
                          cudaStream_t s);
+int launch_round_meta(const int32_t* act, int n, const int32_t* pos, int max_batch, int cols, int item_tokens,
+                      int32_t* out, cudaStream_t s);
+int launch_round_advance(const int32_t* act, int n, const int32_t* acc, int32_t* pos, int max_batch, cudaStream_t s);
 int launch_keys_to_ids(const unsigned long long* keys, int32_t* ids, int n, cudaStream_t s);
 int launch_argmax_rows(int dtype, const void* logits, int n, int vocab, int32_t* ids, cudaStream_t s);
 int launch_swiglu_f32(const float* gu, float* out, int n, int inter, cudaStream_t s);

@@ -489,6 +489,26 @@ int eesd_greedy_accept(const int32_t* y, const int32_t* vinfo, int nv, int32_t* 
   return rc ? fail(rc, "greedy_accept launch") : EESD_OK;
 }
 
+size_t eesd_round_meta_ints(int n, int gamma, int item_tokens) {
+  if (n < 0 || gamma < 0 || item_tokens <= 0) return 0;
+  const size_t cols = (size_t)gamma + 1, ni = (cols + item_tokens - 1) / item_tokens;
+  return cols * 10 * (size_t)n + (size_t)n * (3 * cols + 4 + 2 * ni + 3);
+}
+
+int eesd_round_meta(const int32_t* act, int n, const int32_t* pos, int max_batch, int gamma, int item_tokens,
+                    int32_t* out, void* stream) {
+  if (!act || !pos || !out || n < 0 || max_batch <= 0 || gamma < 0 || item_tokens <= 0)
+    return fail(EESD_ERR_ARG, "round_meta arguments");
+  const int rc = launch_round_meta(act, n, pos, max_batch, gamma + 1, item_tokens, out, static_cast<cudaStream_t>(stream));
+  return rc ? fail(rc, "round_meta launch") : EESD_OK;
+}
+
+int eesd_round_advance(const int32_t* act, int n, const int32_t* acc, int32_t* pos, int max_batch, void* stream) {
+  if (!act || !acc || !pos || n < 0 || max_batch <= 0) return fail(EESD_ERR_ARG, "round_advance arguments");
+  const int rc = launch_round_advance(act, n, acc, pos, max_batch, static_cast<cudaStream_t>(stream));
+  return rc ? fail(rc, "round_advance launch") : EESD_OK;
+}
+
 int eesd_rmsnorm(int dtype, const void* x, const int32_t* rows, const void* w, void* y, int n, int dim, float eps,
                  void* stream) {
   if (!x || !w || !y || n < 0 || dim <= 0) return fail(EESD_ERR_ARG, "rmsnorm arguments");

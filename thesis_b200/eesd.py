@@ -134,7 +134,7 @@ class B200SpecEngine(_B200Engine):
     name = "b200_layerskip"
 
     def __init__(self, model, batch_size, max_prompt_len, max_new_tokens, eos_ids, *, exit_layer: int, gamma: int,
-                 **kw):
+                 overlap: bool = True, **kw):
         w = as_weights(model)
         if not 1 <= exit_layer < w.cfg.n_layers:
             raise ValueError(f"exit_layer must be in [1, {w.cfg.n_layers - 1}]")
@@ -151,6 +151,33 @@ class B200SpecEngine(_B200Engine):
         self.stats = {"rounds": 0, "request_rounds": 0, "drafted": 0, "accepted": 0, "rejected": 0,
                       "overdraft_steps": 0, "full_accept_rounds": 0}
         self.accept_hist = np.zeros(self.gamma + 1, dtype=np.int64)
+        # overlapped rounds: round r+1 is enqueued before round r's acceptance is read back; its
+        # metadata and positions are built on the device (eesd_round_meta / eesd_round_advance)
+        self.overlap = bool(overlap) and type(self)._iteration is B200SpecEngine._iteration
+        self.pos_dev = torch.zeros(self.B, dtype=torch.int32, device=self.device)
+        L = lib.load()
+        self.meta_ints = int(L.eesd_round_meta_ints(self.B, self.gamma, self.dm.item_tokens))
+        self.meta_dev = torch.empty(self.meta_ints, dtype=torch.int32, device=self.device)
+        self.out_hosts = [self.out_host, torch.empty_like(self.out_host).pin_memory()]
+        self.gen = [0] * self.B            # assignment count per slot: stale in-flight results are dropped
+        self.inflight: list = []
+        self.round_seq = 0
+
+    def _on_assigned(self, slot: int) -> None:
+        self.gen[slot] += 1
+
+    def _prefill_slots(self, prompts: dict) -> dict:
+        first = super()._prefill_slots(prompts)
+        slots = sorted(first)
+        lens = np.array([len(prompts[s]) for s in slots], dtype=np.int32)
+        _, (len_d, idx_d) = self.dm.upload(self.dm.pack([(0, 0, 1)]), (lens, np.array(slots, dtype=np.int32)))
+        lib.call("eesd_scatter_ids", len_d.data_ptr(), idx_d.data_ptr(), self.pos_dev.data_ptr(), len(slots),
+                 lib.stream_ptr())
+        return first
+
+    def free(self) -> None:
+        self.inflight.clear()
+        super().free()
 
     # ---------------------------------------------------------------- one round
     def _shallow(self, act: list, pos: np.ndarray, j: int, draft: bool):
@@ -175,6 +202,11 @@ class B200SpecEngine(_B200Engine):
 
     @torch.inference_mode()
     def _iteration(self, measured: bool) -> int:
+        if self.overlap:
+            return self._iteration_overlapped(measured)
+        return self._iteration_sync(measured)
+
+    def _iteration_sync(self, measured: bool) -> int:
         dm, g, cols = self.dm, self.gamma, self.cols
         act = self._active()
         n = len(act)
@@ -224,6 +256,111 @@ class B200SpecEngine(_B200Engine):
             st.last_token = int(y_h[v, a])
             committed += self._commit(s, y_h[v, :a + 1].tolist())
             if measured and st.finish_reason is None:
+                S = self.stats
+                S["request_rounds"] += 1
+                S["drafted"] += g
+                S["accepted"] += a
+                S["rejected"] += g - a
+                S["overdraft_steps"] += max(g - a - 1, 0)
+                S["full_accept_rounds"] += int(a == g)
+                self.accept_hist[a] += 1
+        return committed
+
+    # ---------------------------------------------------------------- overlapped rounds
+    def _iteration_overlapped(self, measured: bool) -> int:
+        """Enqueue this round, then commit the previous one: the host's bookkeeping and the
+        read-back wait overlap the device's work on the next round.  A request that finished in
+        the previous round runs one extra (discarded) round; its positions stay inside the
+        engine's spec slack."""
+        act = [s for s in self._active() if self.slots[s].finish_reason is None]
+        if act:
+            self.inflight.append(self._enqueue_round(act, measured))
+        committed = 0
+        while len(self.inflight) > (1 if act else 0):
+            committed += self._commit_round(self.inflight.pop(0))
+        return committed
+
+    def _enqueue_round(self, act: list, measured: bool) -> dict:
+        dm, g, cols, L = self.dm, self.gamma, self.cols, self.cfg.n_layers
+        n, it = len(act), dm.item_tokens
+        ni = -(-cols // it)
+        sp = lib.stream_ptr()
+        act_np = np.array(act, dtype=np.int32)
+        _, (act_d,) = dm.upload(dm.pack([(0, 0, 1)]), (act_np,))
+        self.h2d_bytes += 4 * (n + 7)
+        base = self.meta_dev.data_ptr()
+        lib.call("eesd_round_meta", act_d.data_ptr(), n, self.pos_dev.data_ptr(), self.B, g, it, base, sp)
+        # host bound on this round's keys: positions lag at most one round (cols) behind the device
+        max_ctx = min(max(self.slots[s].pos for s in act) + 2 * cols, dm.max_seq)
+        dt = lib.BF16 if self.weights.dtype == torch.bfloat16 else lib.F32
+        ivs = []
+        for j in range(cols):
+            o = base + 4 * j * 10 * n
+            b = lib.Batch(n, n, n, max_ctx, o, o + 4 * n, o + 8 * n, o + 24 * n)
+            src, dst = o + 32 * n, o + 36 * n
+            iv = Interval(self.device).start() if j < g else None
+            if j == g:
+                iv_v = Interval(self.device).start()
+            ids = torch.empty(n, dtype=torch.int32, device=self.device)
+            lib.call("eesd_gather_ids", self.seq_buf.data_ptr(), src, ids.data_ptr(), n, sp)
+            x = dm.embed(ids, out=self.xbuf[:n])
+            dm.forward_layers(x, b, 0, self.k)
+            lib.call("eesd_copy_rows", dt, x.data_ptr(), None, self.exit_h.data_ptr(), src, n, self.cfg.dim, sp)
+            if j < g:
+                d = dm.head_argmax(x)
+                lib.call("eesd_scatter_ids", d.data_ptr(), dst, self.seq_buf.data_ptr(), n, sp)
+                iv.stop()
+                ivs.append(("draft", iv, n, n, 0))
+        # verify: gamma + 1 tokens per request from their exit-layer states through [E, L)
+        N = n * cols
+        v = base + 4 * cols * 10 * n
+        vblk = v + 4 * 2 * N
+        vitems = vblk + 4 * 4 * n
+        vrows = vitems + 4 * 2 * n * ni
+        vinfo = vrows + 4 * N
+        b = lib.Batch(N, n, n * ni, max_ctx, v, v + 4 * N, vblk, vitems)
+        x = self.xbuf[:N]
+        lib.call("eesd_copy_rows", dt, self.exit_h.data_ptr(), vrows, x.data_ptr(), None, N, self.cfg.dim, sp)
+        dm.forward_layers(x, b, self.k, L)
+        acc = self.out[:n]
+        y = self.out[n:n + N]
+        dm.head_argmax(x, out=y)
+        lib.call("eesd_greedy_accept", y.data_ptr(), vinfo, n, self.seq_buf.data_ptr(), cols, acc.data_ptr(), sp)
+        lib.call("eesd_round_advance", act_d.data_ptr(), n, acc.data_ptr(), self.pos_dev.data_ptr(), self.B, sp)
+        iv_v.stop()
+        ivs.append(("verify", iv_v, n, n, N))
+        host = self.out_hosts[self.round_seq % 2]     # two pinned buffers: one round read, one in flight
+        self.round_seq += 1
+        host[:n + N].copy_(self.out[:n + N], non_blocking=True)
+        done = torch.cuda.Event()
+        done.record()
+        self.d2h_bytes += 4 * (n + N)
+        kv = int(sum(self.slots[s].pos for s in act)) + n * cols
+        return {"act": act, "gens": [self.gen[s] for s in act], "host": host, "event": done, "ivs": ivs,
+                "measured": measured, "n": n, "N": N, "kv": kv}
+
+    def _commit_round(self, r: dict) -> int:
+        r["event"].synchronize()          # this round's read-back (the next round is already queued)
+        g, cols, n, N = self.gamma, self.cols, r["n"], r["N"]
+        out = r["host"].numpy()
+        acc_h, y_h = out[:n], out[n:n + N].reshape(n, cols)
+        live = [self.gen[s] == gn and not self.slots[s].idle and self.slots[s].finish_reason is None
+                for s, gn in zip(r["act"], r["gens"])]
+        if not any(live):
+            return 0                          # every request of this round had finished before it was read
+        self.stats["rounds"] += 1
+        for kind, iv, bb, st_, dt in r["ivs"]:
+            self.records.append(StepRecord(kind, iv.ms, bb, st_, dt, r["kv"], r["measured"]))
+        committed = 0
+        for v, s in enumerate(r["act"]):
+            st = self.slots[s]
+            if not live[v]:
+                continue                      # finished (or reassigned) before this round was read
+            a = int(acc_h[v])
+            st.pos = st.pos + a + 1
+            st.last_token = int(y_h[v, a])
+            committed += self._commit(s, y_h[v, :a + 1].tolist())
+            if r["measured"] and st.finish_reason is None:
                 S = self.stats
                 S["request_rounds"] += 1
                 S["drafted"] += g

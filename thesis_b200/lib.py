@@ -59,6 +59,9 @@ SIGNATURES = {
     "eesd_gather_ids": (C.c_int, [vp, vp, vp, C.c_int, vp]),
     "eesd_scatter_ids": (C.c_int, [vp, vp, vp, C.c_int, vp]),
     "eesd_greedy_accept": (C.c_int, [vp, vp, C.c_int, vp, C.c_int, vp, vp]),
+    "eesd_round_meta_ints": (sz, [C.c_int, C.c_int, C.c_int]),
+    "eesd_round_meta": (C.c_int, [vp, C.c_int, vp, C.c_int, C.c_int, C.c_int, vp, vp]),
+    "eesd_round_advance": (C.c_int, [vp, C.c_int, vp, vp, C.c_int, vp]),
     "eesd_rmsnorm": (C.c_int, [C.c_int, vp, vp, vp, vp, C.c_int, C.c_int, C.c_float, vp]),
     "eesd_gemm_workspace_bytes": (sz, [C.c_int, C.c_int, C.c_int, C.c_int]),
     "eesd_gemm": (C.c_int, [C.c_int, C.c_int, vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, vp, sz, vp]),
@@ -96,7 +99,8 @@ def check(rc: int, what: str = "") -> None:
 
 
 # entry points that launch exactly one kernel (counted for the bench's launch total)
-KERNEL_CALLS = {"eesd_pack_weight", "eesd_copy_rows", "eesd_gather_ids", "eesd_scatter_ids", "eesd_greedy_accept", "eesd_rmsnorm",
+KERNEL_CALLS = {"eesd_pack_weight", "eesd_copy_rows", "eesd_gather_ids", "eesd_scatter_ids", "eesd_greedy_accept",
+                "eesd_round_meta", "eesd_round_advance", "eesd_rmsnorm",
                 "eesd_gemm"}
 direct_launches = 0
 
