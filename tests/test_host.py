@@ -136,3 +136,36 @@ def test_synthetic_inputs_are_seeded():
     W2 = synthetic_weights(cfg, seed=0)
     assert np.allclose(W["l3.wo"], 0.1 * W2["l3.wo"]) and np.array_equal(W["l2.wo"], W2["l2.wo"])
     assert W["l0.wqkv"].shape == (4 * 64 + 2 * 2 * 64, 256) and W["l0.w13"].shape == (2 * 512, 256)
+
+
+def test_plugin_registers_into_the_reference_harness():
+    """The drop-in boundary itself: the reference's registry takes the B200 methods through
+    ``load_plugins`` and its benchmark parser accepts their flags next to the reference's own.
+    Needs a checkout of the reference (THESIS_REFERENCE); the CUDA library is not touched."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    ref = Path(os.environ.get("THESIS_REFERENCE", "/root/reference"))
+    if not (ref / "common" / "methods.py").exists():
+        pytest.skip("no checkout of the reference")
+    repo = Path(__file__).resolve().parents[1]
+    code = f"""
+import sys
+sys.path[:0] = [{str(ref)!r}, {str(repo)!r}]
+from common.methods import METHODS, load_plugins
+load_plugins(["thesis_b200.plugin"])
+assert {{"b200_autoregressive", "b200_layerskip", "b200_layerskip_dynamic"}} <= set(METHODS), sorted(METHODS)
+from evaluation.benchmark import build_parser
+ap = build_parser()
+a = ap.parse_args(["--method", "b200_layerskip", "--exit-layer", "8", "--gamma", "4"])
+spec = METHODS[a.method]
+assert spec.tag(a) == "-k8-g4" and spec.step_tokens(a) == 5 and spec.params(a) == {{"exit_layer": 8, "gamma": 4}}
+a = ap.parse_args(["--method", "b200_layerskip_dynamic", "--b200-exit-layers", "4,8,12", "--b200-gamma-range", "2,8"])
+assert METHODS[a.method].step_tokens(a) == 9
+print("registered", sorted(m for m in METHODS if m.startswith("b200")))
+"""
+    r = subprocess.run([sys.executable, "-c", code], cwd=str(ref), capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-3000:]
+    assert "b200_layerskip_dynamic" in r.stdout
