@@ -35,7 +35,8 @@ def test_packing_metadata():
 def test_registry_contract():
     from thesis_b200 import methods
 
-    assert {"b200_autoregressive", "b200_layerskip", "b200_layerskip_dynamic"} <= set(methods.METHODS)
+    assert {"b200_autoregressive", "b200_layerskip", "b200_layerskip_dynamic",
+            "b200_layerskip_piggyback"} <= set(methods.METHODS)
     with pytest.raises(ValueError):
         methods.register(methods.METHODS["b200_layerskip"])
     # the CLI groups coexist with a parser that already has --exit-layer / --gamma (the reference's)
@@ -52,6 +53,9 @@ def test_registry_contract():
     dyn = methods.METHODS["b200_layerskip_dynamic"]
     assert dyn.step_tokens(a) == 9 and dyn.tag(a) == "-e4_8_12-g2_8"
     assert dyn.params(a) == {"exit_layers": [4, 8, 12], "gamma_range": [2, 8], "policy_seed": 0}
+    a = ap.parse_args(["--exit-layer", "8", "--b200-piggyback-budget", "128"])
+    pb = methods.METHODS["b200_layerskip_piggyback"]
+    assert pb.tag(a) == "-k8-g4-pb128" and pb.step_tokens(a) == 5
 
 
 class ToyEngine(DecodeEngine):

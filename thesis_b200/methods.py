@@ -111,12 +111,34 @@ def _b200_dyn_build(model, args, batch_size, max_prompt_len, eos):
                                  policy_seed=args.b200_policy_seed, **_kw(args))
 
 
+def _b200_piggy_args(g) -> None:
+    _b200_spec_args(g)
+    if not _has(g, "--b200-piggyback-budget"):
+        g.add_argument("--b200-piggyback-budget", type=int, default=256,
+                       help="[b200_layerskip_piggyback] prompt tokens carried by each shallow step")
+
+
+def _b200_piggy_build(model, args, batch_size, max_prompt_len, eos):
+    from .serving import B200ServingEngine
+
+    if args.exit_layer is None:
+        raise SystemExit("--exit-layer is required for b200_layerskip_piggyback")
+    return B200ServingEngine(model, batch_size, max_prompt_len, args.max_new_tokens, eos, exit_layer=args.exit_layer,
+                             gamma=args.gamma, piggyback_budget=args.b200_piggyback_budget, **_kw(args))
+
+
 SPECS = [
     MethodSpec("b200_autoregressive", "all N layers per token on the sm_100a packed path (lossless reference)",
                _b200_ar_args, _b200_ar_build),
     MethodSpec("b200_layerskip", "synchronous batched LayerSkip on the sm_100a packed path (fixed E, gamma)",
                _b200_spec_args, _b200_spec_build, tag=lambda a: f"-k{a.exit_layer}-g{a.gamma}", spec_slack=64,
                step_tokens=lambda a: a.gamma + 1, params=lambda a: {"exit_layer": a.exit_layer, "gamma": a.gamma}),
+    MethodSpec("b200_layerskip_piggyback",
+               "LayerSkip (fixed E, gamma) with new-request prefill piggybacked on the draft / verify steps",
+               _b200_piggy_args, _b200_piggy_build, tag=lambda a: f"-k{a.exit_layer}-g{a.gamma}-pb{a.b200_piggyback_budget}",
+               spec_slack=64, step_tokens=lambda a: a.gamma + 1,
+               params=lambda a: {"exit_layer": a.exit_layer, "gamma": a.gamma,
+                                 "piggyback_budget": a.b200_piggyback_budget}),
     MethodSpec("b200_layerskip_dynamic",
                "LayerSkip with a per-request exit layer and per-request draft length, coalesced ragged verify",
                _b200_dyn_args, _b200_dyn_build,
