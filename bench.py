@@ -313,6 +313,19 @@ def run_ours(args) -> None:
     else:
         achieved, peak, unit = by / avg_s / 1e9, pk["hbm_gbs"], "GB/s"
     total_ms = sum(g[1] for g in groups.values())
+    # ---- whole-step rooflines: weight + KV bytes each step must read, over the measured HBM peak
+    # (the north star's "fraction of the weight-plus-KV-bytes HBM roofline")
+    L = cfg.n_layers
+    w_layer = sum(algorithmic(k, 0, cfg, 0.0)[0] for k in ("gemm_qkv", "gemm_o", "gemm_w13", "gemm_w2"))
+    w_head = algorithmic("head", 0, cfg, 0.0)[0]
+    kv_layer = algorithmic("attn", 1, cfg, ctx_mean * B_PER_GPU)[0]      # one layer's KV of the batch
+    draft_bytes = EXIT * (w_layer + kv_layer) + w_head
+    verify_bytes = L * (w_layer + kv_layer) + w_head                    # last draft [0, E) + deep [E, L)
+    hbm = pk["hbm_gbs"] * 1e9
+
+    def step_roof(nbytes, ms):
+        return {"bytes": nbytes, "floor_ms": 1000 * nbytes / hbm, "measured_ms": ms,
+                "frac": (1000 * nbytes / hbm) / ms if ms else None}
     share = {f"{k}@{n}": round(v[1] / total_ms, 4) for (k, n), v in sorted(groups.items(), key=lambda kv: -kv[1][1])}
 
     # ---- end to end through the public engine API (host prompts in, token lists out)
@@ -368,6 +381,13 @@ def run_ours(args) -> None:
                          "launches": dcount, "avg_ms": avg_s * 1000, "peak_source": pk["source"],
                          "timing": f"per-launch CUDA events over {args.profile_rounds} profiled rounds after the timed region"},
             "kernel_time_share": share,
+            "step_roofline": {
+                "peak_gbs": pk["hbm_gbs"], "peak_source": pk["source"],
+                "verify": step_roof(verify_bytes, statistics.median(verify) if verify else None),
+                "draft": step_roof(draft_bytes, statistics.median(draft) if draft else None),
+                "round": step_roof(GAMMA * draft_bytes + verify_bytes, ms_max / args.steps),
+                "bytes_are": "bf16 weights of the layers each step runs + LM head + the batch's KV cache at the mean "
+                             "context; activations excluded"},
             "e2e": e2e,
             "cpu_baseline": cb,
         }
