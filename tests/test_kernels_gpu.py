@@ -181,3 +181,46 @@ def test_layer_is_batch_invariant_across_step_shapes(cuda_dev, pos0):
         dm.forward_layers(xd, dm.upload(dm.pack([(0, pos0 + j, 1)])), 0, 1)
         assert torch.equal(xd[0], xv[j]), j
     dm.check()
+
+
+@pytest.mark.parametrize("gamma,item_tokens", [(4, 8), (6, 4), (0, 8)])
+def test_round_metadata_matches_host_packing(cuda_dev, gamma, item_tokens):
+    """The device-built round metadata (eesd_round_meta) equals what the host packing builds for
+    the same blocks, and eesd_round_advance moves each row by its accepted drafts + 1."""
+    from thesis_b200.packing import pack
+
+    cols = gamma + 1
+    act = np.array([5, 0, 3, 7], dtype=np.int32)
+    pos = np.arange(8, dtype=np.int32) * 37 + 100
+    n = len(act)
+    L = lib.load()
+    ints = L.eesd_round_meta_ints(n, gamma, item_tokens)
+    out = torch.zeros(ints, dtype=torch.int32, device=cuda_dev)
+    act_d = torch.from_numpy(act).to(cuda_dev)
+    pos_d = torch.from_numpy(pos).to(cuda_dev)
+    lib.call("eesd_round_meta", act_d.data_ptr(), n, pos_d.data_ptr(), 8, gamma, item_tokens, out.data_ptr(),
+             lib.stream_ptr())
+    o = out.cpu().numpy()
+    for j in range(cols):
+        st = o[j * 10 * n:(j + 1) * 10 * n]
+        ph = pack([(int(r), int(pos[r]) + j, 1) for r in act], item_tokens)
+        assert np.array_equal(st[:n], ph.tok_pos) and np.array_equal(st[n:2 * n], ph.tok_row)
+        assert np.array_equal(st[2 * n:6 * n].reshape(n, 4), ph.blk)
+        assert sorted(map(tuple, st[6 * n:8 * n].reshape(n, 2))) == sorted(map(tuple, ph.items))
+        assert np.array_equal(st[8 * n:9 * n], act * cols + j) and np.array_equal(st[9 * n:], act * cols + j + 1)
+    v = o[cols * 10 * n:]
+    N, ni = n * cols, -(-cols // item_tokens)
+    ph = pack([(int(r), int(pos[r]), cols) for r in act], item_tokens)
+    assert np.array_equal(v[:N], ph.tok_pos) and np.array_equal(v[N:2 * N], ph.tok_row)
+    assert np.array_equal(v[2 * N:2 * N + 4 * n].reshape(n, 4), ph.blk)
+    items = v[2 * N + 4 * n:2 * N + 4 * n + 2 * n * ni].reshape(-1, 2)
+    assert sorted(map(tuple, items)) == sorted(map(tuple, ph.items))
+    rows = v[2 * N + 4 * n + 2 * n * ni:3 * N + 4 * n + 2 * n * ni]
+    assert np.array_equal(rows, (act[:, None] * cols + np.arange(cols)[None, :]).reshape(-1))
+    vinfo = v[3 * N + 4 * n + 2 * n * ni:].reshape(n, 3)
+    assert np.array_equal(vinfo, np.stack([np.arange(n) * cols, np.full(n, cols), act], axis=1))
+    acc = torch.tensor([0, 3, 1, 2], dtype=torch.int32, device=cuda_dev)
+    lib.call("eesd_round_advance", act_d.data_ptr(), n, acc.data_ptr(), pos_d.data_ptr(), 8, lib.stream_ptr())
+    want = pos.copy()
+    want[act] += acc.cpu().numpy() + 1
+    assert np.array_equal(pos_d.cpu().numpy(), want)
