@@ -56,6 +56,19 @@ def test_eos_stops_generation(c1s_bf16, ar_reference):
     assert ar["p0"][-1] == eos and len(ar["p0"]) <= 6
 
 
+@pytest.mark.parametrize("kw", [{}, {"exit_layer": 3, "gamma": 4}])
+def test_overlapped_steps_equal_synchronous_steps(c1s_bf16, ar_reference, kw):
+    """Enqueueing step k+1 before reading step k back changes nothing: same tokens with EOS stops
+    and slot refills (6 prompts through 2 slots), AR and speculative alike."""
+    prompts, ref = ar_reference
+    eos = ref["p1"][7]
+    cls = B200SpecEngine if kw else B200ARBatchEngine
+    rc = RunConfig(mode="static", keep_outputs=True)
+    outs = [_outputs(cls(c1s_bf16, 2, 60, MAX_NEW, (eos,), overlap=o, **kw).run(prompts, rc)) for o in (True, False)]
+    assert outs[0] == outs[1]
+    assert len(outs[0]["p1"]) <= 8 and outs[0]["p1"][-1] == eos
+
+
 def test_cyclic_run_converges_and_reports(c1s_bf16):
     prompts = synthetic_prompts(4, c1s_bf16.cfg.vocab_size, seed=2, min_len=5, max_len=20)
     eng = B200SpecEngine(c1s_bf16, 3, 20, 12, (2,), ignore_eos=True, exit_layer=4, gamma=3)

@@ -51,6 +51,7 @@ def as_weights(model) -> ModelWeights:
 
 class _B200Engine(DecodeEngine):
     cols = 1
+    pos_dev = None                 # device positions, for engines that run overlapped steps
 
     def __init__(self, model, batch_size, max_prompt_len, max_new_tokens, eos_ids, *, step_tokens: int = 1,
                  prefill_budget: int = 2048, prefill_chunk: int = 512, extra_tokens: int = 0, **kw):
@@ -81,26 +82,125 @@ class _B200Engine(DecodeEngine):
         (EESDEngine.step, solutions/engine.py:237-242)."""
         return self._iteration(measured)
 
-    def free(self) -> None:
-        self.dm.close()
-
     def _prefill_slots(self, prompts: dict) -> dict:
         first = self.dm.prefill(prompts, chunk=self.prefill_chunk)
         slots = sorted(first)
         ids = np.array([first[s] for s in slots], dtype=np.int32)
         idx = np.array([s * self.cols for s in slots], dtype=np.int32)
-        ph = self.dm.pack([(0, 0, 1)])          # metadata slot carrying the two index arrays
-        _, (ids_d, idx_d) = self.dm.upload(ph, (ids, idx))
-        lib.call("eesd_scatter_ids", ids_d.data_ptr(), idx_d.data_ptr(), self.seq_buf.data_ptr(), len(slots),
-                 lib.stream_ptr())
+        lens = np.array([len(prompts[s]) for s in slots], dtype=np.int32)
+        ph = self.dm.pack([(0, 0, 1)])          # metadata slot carrying the index arrays
+        _, (ids_d, idx_d, len_d, row_d) = self.dm.upload(ph, (ids, idx, lens, np.array(slots, dtype=np.int32)))
+        sp = lib.stream_ptr()
+        lib.call("eesd_scatter_ids", ids_d.data_ptr(), idx_d.data_ptr(), self.seq_buf.data_ptr(), len(slots), sp)
+        if self.pos_dev is not None:
+            # device-resident positions of the overlapped steps (the prompt length is the first decode position)
+            lib.call("eesd_scatter_ids", len_d.data_ptr(), row_d.data_ptr(), self.pos_dev.data_ptr(), len(slots), sp)
         return first
+
+    # ---------------------------------------------------------------- overlapped steps
+    # Step k+1 is enqueued before step k is read back: positions live on the device
+    # (eesd_round_meta builds the packed metadata from them, eesd_round_advance moves them), the
+    # host keeps two pinned read-back buffers and commits a step one iteration later.  A request
+    # that finished in step k runs one more (discarded) step, inside the engine's spec slack; a
+    # slot reassigned meanwhile is recognised by its assignment count.
+    def _init_overlap(self, overlap: bool, gamma: int) -> None:
+        self.overlap = bool(overlap)
+        self.pos_dev = torch.zeros(self.B, dtype=torch.int32, device=self.device)
+        self.meta_ints = int(lib.load().eesd_round_meta_ints(self.B, gamma, self.dm.item_tokens))
+        self.meta_dev = torch.empty(self.meta_ints, dtype=torch.int32, device=self.device)
+        self.gen = [0] * self.B            # assignment count per slot: stale in-flight results are dropped
+        self.inflight: list = []
+        self.round_seq = 0
+
+    def _on_assigned(self, slot: int) -> None:
+        self.gen[slot] += 1
+
+    def _overlapped(self, measured: bool) -> int:
+        """Enqueue this step, then commit the previous one."""
+        act = [s for s in self._active() if self.slots[s].finish_reason is None]
+        if act:
+            self.inflight.append(self._enqueue_round(act, measured))
+        committed = 0
+        while len(self.inflight) > (1 if act else 0):
+            committed += self._commit_round(self.inflight.pop(0))
+        return committed
+
+    def _live(self, r: dict) -> list:
+        return [self.gen[s] == gn and not self.slots[s].idle and self.slots[s].finish_reason is None
+                for s, gn in zip(r["act"], r["gens"])]
+
+    def free(self) -> None:
+        if hasattr(self, "inflight"):
+            self.inflight.clear()
+        self.dm.close()
 
 
 class B200ARBatchEngine(_B200Engine):
     name = "b200_autoregressive"
 
+    def __init__(self, model, batch_size, max_prompt_len, max_new_tokens, eos_ids, *, overlap: bool = True, **kw):
+        kw.setdefault("spec_slack", 32)
+        super().__init__(model, batch_size, max_prompt_len, max_new_tokens, eos_ids, **kw)
+        self._init_overlap(overlap, 0)
+        self.zeros_dev = torch.zeros(self.B, dtype=torch.int32, device=self.device)
+        self.y_dev = torch.empty(self.B, dtype=torch.int32, device=self.device)
+        self.y_hosts = [torch.empty(self.B, dtype=torch.int32).pin_memory() for _ in range(2)]
+
     @torch.inference_mode()
     def _iteration(self, measured: bool) -> int:
+        return self._overlapped(measured) if self.overlap else self._iteration_sync(measured)
+
+    def _enqueue_round(self, act: list, measured: bool) -> dict:
+        """One token per request through all layers + head; the token is the next step's input."""
+        dm, n = self.dm, len(act)
+        sp = lib.stream_ptr()
+        _, (act_d,) = dm.upload(dm.pack([(0, 0, 1)]), (np.array(act, dtype=np.int32),))
+        self.h2d_bytes += 4 * (n + 7)
+        base = self.meta_dev.data_ptr()
+        iv = Interval(self.device).start()
+        lib.call("eesd_round_meta", act_d.data_ptr(), n, self.pos_dev.data_ptr(), self.B, 0, dm.item_tokens, base, sp)
+        max_ctx = min(max(self.slots[s].pos for s in act) + 2, dm.max_seq)
+        b = lib.Batch(n, n, n, max_ctx, base, base + 4 * n, base + 8 * n, base + 24 * n)
+        src = base + 32 * n
+        ids = torch.empty(n, dtype=torch.int32, device=self.device)
+        lib.call("eesd_gather_ids", self.seq_buf.data_ptr(), src, ids.data_ptr(), n, sp)
+        x = dm.embed(ids)
+        dm.forward_layers(x, b, 0, self.cfg.n_layers)
+        y = self.y_dev[:n]
+        dm.head_argmax(x, out=y)
+        lib.call("eesd_scatter_ids", y.data_ptr(), src, self.seq_buf.data_ptr(), n, sp)
+        lib.call("eesd_round_advance", act_d.data_ptr(), n, self.zeros_dev.data_ptr(), self.pos_dev.data_ptr(), self.B,
+                 sp)
+        iv.stop()
+        host = self.y_hosts[self.round_seq % 2]
+        self.round_seq += 1
+        host[:n].copy_(y, non_blocking=True)
+        done = torch.cuda.Event()
+        done.record()
+        self.d2h_bytes += 4 * n
+        kv = int(sum(self.slots[s].pos for s in act)) + n
+        return {"act": act, "gens": [self.gen[s] for s in act], "host": host, "event": done, "iv": iv,
+                "measured": measured, "n": n, "kv": kv}
+
+    def _commit_round(self, r: dict) -> int:
+        r["event"].synchronize()
+        live = self._live(r)
+        if not any(live):
+            return 0
+        n = r["n"]
+        self.records.append(StepRecord("ar", r["iv"].ms, n, n, n, r["kv"], r["measured"]))
+        y_h = r["host"][:n].tolist()
+        committed = 0
+        for v, (s, t) in enumerate(zip(r["act"], y_h)):
+            if not live[v]:
+                continue
+            st = self.slots[s]
+            st.pos += 1
+            st.last_token = t
+            committed += self._commit(s, [t])
+        return committed
+
+    def _iteration_sync(self, measured: bool) -> int:
         dm = self.dm
         act = self._active()
         n = len(act)
@@ -153,31 +253,8 @@ class B200SpecEngine(_B200Engine):
         self.accept_hist = np.zeros(self.gamma + 1, dtype=np.int64)
         # overlapped rounds: round r+1 is enqueued before round r's acceptance is read back; its
         # metadata and positions are built on the device (eesd_round_meta / eesd_round_advance)
-        self.overlap = bool(overlap) and type(self)._iteration is B200SpecEngine._iteration
-        self.pos_dev = torch.zeros(self.B, dtype=torch.int32, device=self.device)
-        L = lib.load()
-        self.meta_ints = int(L.eesd_round_meta_ints(self.B, self.gamma, self.dm.item_tokens))
-        self.meta_dev = torch.empty(self.meta_ints, dtype=torch.int32, device=self.device)
+        self._init_overlap(overlap and type(self)._iteration is B200SpecEngine._iteration, self.gamma)
         self.out_hosts = [self.out_host, torch.empty_like(self.out_host).pin_memory()]
-        self.gen = [0] * self.B            # assignment count per slot: stale in-flight results are dropped
-        self.inflight: list = []
-        self.round_seq = 0
-
-    def _on_assigned(self, slot: int) -> None:
-        self.gen[slot] += 1
-
-    def _prefill_slots(self, prompts: dict) -> dict:
-        first = super()._prefill_slots(prompts)
-        slots = sorted(first)
-        lens = np.array([len(prompts[s]) for s in slots], dtype=np.int32)
-        _, (len_d, idx_d) = self.dm.upload(self.dm.pack([(0, 0, 1)]), (lens, np.array(slots, dtype=np.int32)))
-        lib.call("eesd_scatter_ids", len_d.data_ptr(), idx_d.data_ptr(), self.pos_dev.data_ptr(), len(slots),
-                 lib.stream_ptr())
-        return first
-
-    def free(self) -> None:
-        self.inflight.clear()
-        super().free()
 
     # ---------------------------------------------------------------- one round
     def _shallow(self, act: list, pos: np.ndarray, j: int, draft: bool):
@@ -202,9 +279,7 @@ class B200SpecEngine(_B200Engine):
 
     @torch.inference_mode()
     def _iteration(self, measured: bool) -> int:
-        if self.overlap:
-            return self._iteration_overlapped(measured)
-        return self._iteration_sync(measured)
+        return self._overlapped(measured) if self.overlap else self._iteration_sync(measured)
 
     def _iteration_sync(self, measured: bool) -> int:
         dm, g, cols = self.dm, self.gamma, self.cols
@@ -267,19 +342,6 @@ class B200SpecEngine(_B200Engine):
         return committed
 
     # ---------------------------------------------------------------- overlapped rounds
-    def _iteration_overlapped(self, measured: bool) -> int:
-        """Enqueue this round, then commit the previous one: the host's bookkeeping and the
-        read-back wait overlap the device's work on the next round.  A request that finished in
-        the previous round runs one extra (discarded) round; its positions stay inside the
-        engine's spec slack."""
-        act = [s for s in self._active() if self.slots[s].finish_reason is None]
-        if act:
-            self.inflight.append(self._enqueue_round(act, measured))
-        committed = 0
-        while len(self.inflight) > (1 if act else 0):
-            committed += self._commit_round(self.inflight.pop(0))
-        return committed
-
     def _enqueue_round(self, act: list, measured: bool) -> dict:
         dm, g, cols, L = self.dm, self.gamma, self.cols, self.cfg.n_layers
         n, it = len(act), dm.item_tokens
@@ -344,8 +406,7 @@ class B200SpecEngine(_B200Engine):
         g, cols, n, N = self.gamma, self.cols, r["n"], r["N"]
         out = r["host"].numpy()
         acc_h, y_h = out[:n], out[n:n + N].reshape(n, cols)
-        live = [self.gen[s] == gn and not self.slots[s].idle and self.slots[s].finish_reason is None
-                for s, gn in zip(r["act"], r["gens"])]
+        live = self._live(r)
         if not any(live):
             return 0                          # every request of this round had finished before it was read
         self.stats["rounds"] += 1
