@@ -311,7 +311,7 @@ class DeviceModel:
         budget = budget or self.max_tokens
         rows = list(prompts)
         done = {}
-        last_h = {}
+        last_h = []          # (rows, device ids): read back once, after every call is enqueued
         r = 0
         while True:
             chunks = [(row, r * chunk, min(chunk, len(prompts[row]) - r * chunk)) for row in rows
@@ -327,9 +327,10 @@ class DeviceModel:
                     call.append(c)
                     used += c[2]
             r += 1
-        for row in rows:
-            done[row] = last_h[row]
-        return done
+        for fin, y in last_h:
+            for row, v in zip(fin, y.tolist()):
+                done[row] = v
+        return {row: done[row] for row in rows}
 
     def _prefill_call(self, call, prompts, last_h) -> None:
         if not call:
@@ -343,6 +344,4 @@ class DeviceModel:
         if ends:
             rows_t = torch.tensor(ends, dtype=torch.int32).pin_memory().to(self.device, non_blocking=True)
             y = self.head_argmax(x, rows_t)
-            fin = [row for (row, s, c) in call if s + c == len(prompts[row])]
-            for row, v in zip(fin, y.tolist()):
-                last_h[row] = v
+            last_h.append(([row for (row, s, c) in call if s + c == len(prompts[row])], y))
