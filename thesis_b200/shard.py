@@ -19,32 +19,32 @@ def shard_requests(n: int, rank: int, world: int) -> list:
 
 
 def gather_outputs(outputs: dict, n_total: int, world: int, device=None, group=None) -> dict:
-    """outputs: {request index: token list} of this rank -> {request index: tokens} of all ranks."""
+    """outputs: {request index: token list} of this rank -> {request index: tokens} of all ranks.
+
+    Two ``all_gather`` calls (the [rows, width] of every rank, then the padded blocks) and one
+    read-back of each; the blocks are filled and split with numpy."""
     import torch.distributed as dist
 
     dev = device if device is not None else torch.device("cpu")
     keys = sorted(outputs)
-    max_len = max((len(outputs[k]) for k in keys), default=0)
-    n_local = torch.tensor([len(keys), max_len], dtype=torch.int64, device=dev)
+    lens = np.array([len(outputs[k]) for k in keys], dtype=np.int64)
+    n_local = torch.tensor([len(keys), int(lens.max(initial=0))], dtype=torch.int64, device=dev)
     sizes = [torch.zeros(2, dtype=torch.int64, device=dev) for _ in range(world)]
     dist.all_gather(sizes, n_local, group=group)
-    rows = max(int(s[0]) for s in sizes)
-    width = max(int(s[1]) for s in sizes)
-    block = torch.full((max(rows, 1), width + 2), -1, dtype=torch.int32)
-    for i, k in enumerate(keys):
-        t = outputs[k]
-        block[i, 0] = k
-        block[i, 1] = len(t)
-        block[i, 2:2 + len(t)] = torch.tensor(t, dtype=torch.int32)
-    block = block.to(dev)
-    parts = [torch.empty_like(block) for _ in range(world)]
-    dist.all_gather(parts, block, group=group)
-    out = {}
-    for p in parts:
-        p = p.cpu().numpy()
-        for row in p:
-            if row[0] >= 0:
-                out[int(row[0])] = row[2:2 + int(row[1])].tolist()
+    sz = torch.stack(sizes).cpu().numpy()
+    rows, width = max(int(sz[:, 0].max()), 1), int(sz[:, 1].max())
+    block = np.full((rows, width + 2), -1, dtype=np.int32)
+    if keys:
+        block[:len(keys), 0] = keys
+        block[:len(keys), 1] = lens
+        if width:
+            filled = np.arange(width) < lens[:, None]
+            block[:len(keys), 2:][filled] = np.concatenate([np.asarray(outputs[k], dtype=np.int32) for k in keys])
+    blk = torch.from_numpy(block).to(dev)
+    parts = [torch.empty_like(blk) for _ in range(world)]
+    dist.all_gather(parts, blk, group=group)
+    allb = torch.cat(parts).cpu().numpy()
+    out = {int(row[0]): row[2:2 + int(row[1])].tolist() for row in allb if row[0] >= 0}
     if len(out) != n_total:
         raise RuntimeError(f"gathered {len(out)} of {n_total} requests")
     return out
