@@ -65,11 +65,13 @@ def test_shard_partition():
         shard_requests(3, 4, 4)
 
 
-def test_two_rank_gather_reassembles_every_request():
-    res = _run(2, 7)
+@pytest.mark.parametrize("n", [7, 1])
+def test_two_rank_gather_reassembles_every_request(n):
+    """Ragged outputs, and a rank that owns no request (n = 1)."""
+    res = _run(2, n)
     for rank, status, allo in res:
         assert status == "ok"
-        assert allo == {i: [i] * (i % 4 + 1) for i in range(7)}
+        assert allo == {i: [i] * (i % 4 + 1) for i in range(n)}
 
 
 def test_failed_rank_surfaces_as_an_error_on_the_other_rank():
