@@ -10,9 +10,10 @@ A "step" is one draft/verify round over the GPU's batch: gamma shallow steps (la
 and one verify step (the last draft through [0, 8), then 5 tokens per request through [8, 32) +
 head + greedy acceptance).  Multi-GPU runs shard requests (each rank owns its own 64 requests and
 a full weight replica; weak scaling); the only collective is the final gather of the generated
-tokens (NCCL all_gather) inside the timed region.
+tokens (NCCL all_gather) inside the timed region.  ``--strong`` shards the 64 requests of the
+1-GPU run over the GPUs instead (strong scaling, 64 / N requests per GPU).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--strong]
 
 ``--impl reference`` times the reference algorithm's CPU implementation (the numpy port under
 ``oracle/``, fp32 as the reference runs on CPU) on a bounded sample of the same workload.
@@ -239,9 +240,22 @@ def run_ours(args) -> None:
     cfg = preset("llama3-8b")
     w = ModelWeights.synthetic(cfg, seed=0, dtype=torch.bfloat16, device=dev, residual_scale_from=EXIT,
                                residual_scale=0.1)
-    prompts = synthetic_prompts(B_PER_GPU, cfg.vocab_size, seed=1000 + rank, min_len=PROMPT_LEN[0],
-                                max_len=PROMPT_LEN[1])
-    eng = B200SpecEngine(w, B_PER_GPU, PROMPT_LEN[1], MAX_NEW, (), ignore_eos=True, exit_layer=EXIT, gamma=GAMMA)
+    if args.strong:
+        # strong scaling: the 64 requests of the 1-GPU run, sharded over the ranks
+        from thesis_b200.shard import shard_requests
+
+        allp = synthetic_prompts(B_PER_GPU, cfg.vocab_size, seed=1000, min_len=PROMPT_LEN[0], max_len=PROMPT_LEN[1])
+        ids = shard_requests(B_PER_GPU, rank, world)
+        prompts = [allp[i] for i in ids]
+        n_total = B_PER_GPU
+    else:
+        # weak scaling: 64 requests per GPU
+        prompts = synthetic_prompts(B_PER_GPU, cfg.vocab_size, seed=1000 + rank, min_len=PROMPT_LEN[0],
+                                    max_len=PROMPT_LEN[1])
+        ids = [rank + world * i for i in range(B_PER_GPU)]
+        n_total = B_PER_GPU * world
+    nb = len(prompts)
+    eng = B200SpecEngine(w, nb, PROMPT_LEN[1], MAX_NEW, (), ignore_eos=True, exit_layer=EXIT, gamma=GAMMA)
     eng.start(prompts)
     torch.cuda.synchronize()
     for _ in range(args.warmup):
@@ -253,8 +267,7 @@ def run_ours(args) -> None:
         # it is warmed here like the steps, and runs again inside the timed region
         from thesis_b200.shard import gather_outputs
 
-        gather_outputs({rank + world * i: eng.slots[i].output for i in range(B_PER_GPU)}, B_PER_GPU * world, world,
-                       device=dev)
+        gather_outputs({ids[i]: eng.slots[i].output for i in range(nb)}, n_total, world, device=dev)
     stream = torch.cuda.current_stream()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
@@ -267,8 +280,8 @@ def run_ours(args) -> None:
         for _ in range(args.steps):
             committed += eng.step(measured=True)
         if world > 1:          # final output gather (the only collective): tokens generated so far
-            outs = {rank + world * i: eng.slots[i].output for i in range(B_PER_GPU)}
-            gather_outputs(outs, B_PER_GPU * world, world, device=dev)
+            outs = {ids[i]: eng.slots[i].output for i in range(nb)}
+            gather_outputs(outs, n_total, world, device=dev)
         ev1.record(stream)
         torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
@@ -314,7 +327,7 @@ def run_ours(args) -> None:
     (dk, dn), (dcount, dms) = max(groups.items(), key=lambda kv: kv[1][1])
     pk = peaks()
     ctx_mean = float(np.mean([s.pos for s in eng.slots]))
-    by, fl = algorithmic(dk, dn, cfg, ctx_mean * B_PER_GPU)
+    by, fl = algorithmic(dk, dn, cfg, ctx_mean * nb)
     avg_s = dms / dcount / 1000.0
     tensor_bound = fl / max(by, 1.0) > pk["bf16_tflops_sustained"] * 1e12 / (pk["hbm_gbs"] * 1e9)
     if tensor_bound:
@@ -327,7 +340,7 @@ def run_ours(args) -> None:
     L = cfg.n_layers
     w_layer = sum(algorithmic(k, 0, cfg, 0.0)[0] for k in ("gemm_qkv", "gemm_o", "gemm_w13", "gemm_w2"))
     w_head = algorithmic("head", 0, cfg, 0.0)[0]
-    kv_layer = algorithmic("attn", 1, cfg, ctx_mean * B_PER_GPU)[0]      # one layer's KV of the batch
+    kv_layer = algorithmic("attn", 1, cfg, ctx_mean * nb)[0]      # one layer's KV of the batch
     draft_bytes = EXIT * (w_layer + kv_layer) + w_head
     verify_bytes = L * (w_layer + kv_layer) + w_head                    # last draft [0, E) + deep [E, L)
     hbm = pk["hbm_gbs"] * 1e9
@@ -343,7 +356,7 @@ def run_ours(args) -> None:
         eng.free()
         del eng
         torch.cuda.empty_cache()
-        e2e_eng = B200SpecEngine(w, B_PER_GPU, PROMPT_LEN[1], args.e2e_new, (), ignore_eos=True, exit_layer=EXIT,
+        e2e_eng = B200SpecEngine(w, nb, PROMPT_LEN[1], args.e2e_new, (), ignore_eos=True, exit_layer=EXIT,
                                  gamma=GAMMA)
         if world > 1:
             dist.barrier()
@@ -372,9 +385,11 @@ def run_ours(args) -> None:
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "rank_ms_per_step": rank_ms,
-            "higher_is_better": True, "scaling": "weak",
+            "higher_is_better": True, "scaling": "strong" if args.strong else "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "global_batch": B_PER_GPU * world, "seq_len": MAX_NEW,
+            "config": {"workload": WORKLOAD if not args.strong else WORKLOAD.replace(
+                           "B=64 requests per GPU", f"B=64 requests in total, {nb} per GPU"),
+                       "global_batch": n_total, "seq_len": MAX_NEW,
                        "parallelism": f"request-sharded x{world}" if world > 1 else "single GPU",
                        "l2": "inputs larger than L2: each round streams the 16 GB of weights",
                        "value_is": "aggregate over all GPUs"},
@@ -416,6 +431,8 @@ def main():
     ap.add_argument("--e2e-new", type=int, default=MAX_NEW, help="new tokens per request in the end-to-end run")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--strong", action="store_true",
+                    help="strong scaling: the 64 requests of the 1-GPU run sharded over the GPUs (default: 64 per GPU)")
     ap.add_argument("--profile-rounds", type=int, default=3, help="profiled rounds after the timed region")
     ap.add_argument("--tokens-per-round", type=float, default=3.5 * B_PER_GPU,
                     help="reference arm: tokens committed per round (the GPU engine's measured value)")

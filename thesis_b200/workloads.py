@@ -2,6 +2,7 @@
 
     python -m thesis_b200.workloads c4 [--requests 32] [--new 256]
     python -m thesis_b200.workloads c5 [--requests 256] [--rate 40] [--budget 256]
+    python -m thesis_b200.workloads strong [--rounds 20]
 
 c4  Llama2-7B shape (32 layers, dim 4096, 32 heads MHA of 128, SwiGLU 11008, vocab 32000, RoPE
     theta 10000), bf16, residual outputs of layers >= 4 scaled by 0.1; batch 32, prompt lengths
@@ -14,6 +15,13 @@ c5  Llama3-8B shape, bf16, residual outputs of layers >= 8 scaled by 0.1; 256 sl
     output lengths uniform in 128..1024, exit layer 8, gamma 4, new-request prefill piggybacked
     on the draft/verify steps (``B200ServingEngine.run_poisson``).  Reports throughput, TTFT and
     TPOT of the measured requests.
+
+strong  Strong scaling of config 3 (Llama3-8B shape, E=8, gamma=4, 64 requests in total, prompts
+    U[128,512]) over 1, 2, 4 and 8 GPUs, measured shard by shard on one GPU: ranks share nothing
+    but the final output gather, so an N-GPU run is N independent engines of 64 / N requests
+    (`bench.py --strong --gpus N` runs them concurrently).  For each N every shard runs 3 warm-up
+    and ``--rounds`` timed draft/verify rounds (CUDA events); the aggregate is all shards' tokens
+    over the slowest shard's time, as in the bench.
 
 Weights and prompts are seeded synthetic stand-ins for the checkpoints and datasets the
 reference would use; no dataset item is reproduced.
@@ -90,9 +98,48 @@ def run_c5(args) -> dict:
             "requests_measured": m["evaluated_completions"], "metrics": m}
 
 
+def run_strong(args) -> dict:
+    from .eesd import B200SpecEngine
+    from .shard import shard_requests
+
+    cfg = preset("llama3-8b")
+    w = ModelWeights.synthetic(cfg, seed=0, dtype=torch.bfloat16, device="cuda", residual_scale_from=8,
+                               residual_scale=0.1)
+    allp = synthetic_prompts(64, cfg.vocab_size, seed=1000, min_len=128, max_len=512)
+    rows = []
+    for n in (1, 2, 4, 8):
+        shard_ms, tokens = [], 0
+        for r in range(n):
+            prompts = [allp[i] for i in shard_requests(64, r, n)]
+            eng = B200SpecEngine(w, len(prompts), 512, 512, (), ignore_eos=True, exit_layer=8, gamma=4)
+            eng.start(prompts)
+            for _ in range(3):
+                eng.step(measured=False)
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            got = sum(eng.step(measured=True) for _ in range(args.rounds))
+            b.record()
+            torch.cuda.synchronize()
+            shard_ms.append(a.elapsed_time(b))
+            tokens += got
+            eng.free()
+            del eng
+            torch.cuda.empty_cache()
+        agg = tokens / (max(shard_ms) / 1000.0)
+        rows.append({"gpus": n, "requests_per_gpu": 64 // n, "ms_per_round_max": max(shard_ms) / args.rounds,
+                     "ms_per_round_min": min(shard_ms) / args.rounds, "aggregate_tok_s": agg})
+    for r in rows:
+        r["speedup"] = r["aggregate_tok_s"] / rows[0]["aggregate_tok_s"]
+        r["efficiency"] = r["speedup"] / r["gpus"]
+    return {"workload": "strong", "metric": "generated tokens/s, 64 requests in total (strong scaling)",
+            "unit": "tokens/s", "rounds": args.rounds, "rows": rows}
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("workload", choices=["c4", "c5"])
+    ap.add_argument("workload", choices=["c4", "c5", "strong"])
+    ap.add_argument("--rounds", type=int, default=20)
     ap.add_argument("--requests", type=int, default=None)
     ap.add_argument("--new", type=int, default=256)
     ap.add_argument("--rate", type=float, default=40.0)
@@ -102,7 +149,7 @@ def main(argv=None) -> None:
     args = ap.parse_args(argv)
     if args.requests is None:
         args.requests = 32 if args.workload == "c4" else 256
-    res = run_c4(args) if args.workload == "c4" else run_c5(args)
+    res = {"c4": run_c4, "c5": run_c5, "strong": run_strong}[args.workload](args)
     print(json.dumps(res), flush=True)
 
 
