@@ -262,17 +262,6 @@ __device__ __forceinline__ uint32_t dsmem_addr(uint32_t local, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
   return r;
 }
-// plain loads from cluster shared memory; ordering against the writers comes from cluster_sync
-__device__ __forceinline__ float dsmem_ld_f32(uint32_t addr) {
-  float v;
-  asm("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr));
-  return v;
-}
-__device__ __forceinline__ float2 dsmem_ld_f32x2(uint32_t addr) {
-  float2 v;
-  asm("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr));
-  return v;
-}
 
 __device__ __forceinline__ void set_status(int* status, int bits) {
   if (status) atomicOr(status, bits);

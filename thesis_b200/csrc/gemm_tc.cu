@@ -16,10 +16,10 @@
 // silu(g) * u is formed per thread with no data exchange.
 //
 // Split-K (few output tiles, e.g. the O and W2 projections): the S CTAs that share an output
-// tile form one thread-block cluster (1 x 1 x S).  After the main loop each CTA parks its fp32
-// accumulator in its own shared memory, and CTA r of the cluster sums column slice r of the
-// tile over the S CTAs through distributed shared memory, in split order, then applies the
-// epilogue.  No partial sums touch global memory.
+// tile form one thread-block cluster (1 x 1 x S).  After the main loop each CTA stores the fp32
+// partial sums of the token columns it does not own to a global (L2-resident) scratch, one
+// cluster barrier publishes them, and CTA r sums column slice r over the S splits in split
+// order, then applies the epilogue.
 //
 // Batch invariance (needed for bit-exact speculative == autoregressive output): the K range
 // of every split and the split count depend only on the weight shape, the split sum has a
