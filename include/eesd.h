@@ -201,11 +201,14 @@ int eesd_gemm(int dtype, int epilogue, const void* x, const void* w, const void*
  * changes the summation order, so AR and speculative runs must use the same value).
  * EESD_OPT_STAGES: TMA pipeline depth (0 = as many stages as fit; numerics-neutral).
  * EESD_OPT_PAIR: 1 (default) runs SwiGLU GEMMs on CTA pairs (cta_group::2, M = 256) where the
- * weight shape allows, 0 on single CTAs; AR and speculative runs must use the same value. */
+ * weight shape allows, 0 on single CTAs; AR and speculative runs must use the same value.
+ * EESD_OPT_HEAD_TWO_TILES: 1 (default) lets an LM-head launch of up to 256 tokens take two
+ * 128-row tiles per CTA (two accumulators), 0 one; numerics-neutral. */
 #define EESD_OPT_MMA_N 1
 #define EESD_OPT_SPLITS 2
 #define EESD_OPT_STAGES 3
 #define EESD_OPT_PAIR 4
+#define EESD_OPT_HEAD_TWO_TILES 5
 int eesd_set_option(int option, int value);
 
 /* Exit head that allocates nothing, for callers that cannot call cudaMalloc (a serving

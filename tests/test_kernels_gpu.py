@@ -224,3 +224,42 @@ def test_round_metadata_matches_host_packing(cuda_dev, gamma, item_tokens):
     want = pos.copy()
     want[act] += acc.cpu().numpy() + 1
     assert np.array_equal(pos_d.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("n", [1, 37, 256, 300])
+def test_head_two_row_tiles_per_cta(cuda_dev, n):
+    """Head launches of up to 256 tokens take two 128-row tiles per CTA (two accumulators); a
+    vocabulary of 11 tiles leaves the last CTA half past the end.  The token ids equal the
+    one-tile kernel's and the argmax of the stored logits, through the model head (tile-packed
+    weights) and, up to its 128 rows, the allocation-free head (row-major weights)."""
+    from dataclasses import replace
+
+    from thesis_b200.config import preset
+    from thesis_b200.model import DeviceModel, ModelWeights
+
+    cfg = replace(preset("c1s"), vocab_size=1300, n_layers=1)
+    w = ModelWeights.synthetic(cfg, seed=4, dtype=torch.bfloat16, device=cuda_dev)
+    dm = DeviceModel(w, max_batch=1, max_seq=64, max_tokens=320)
+    g = torch.Generator(device=cuda_dev).manual_seed(n)
+    x = torch.randn(n, cfg.dim, device=cuda_dev, generator=g).bfloat16()
+
+    def static_head():   # its fixed scratch holds up to 128 rows
+        ids = torch.full((n,), -1, dtype=torch.int32, device=cuda_dev)
+        if n > 128:
+            return None
+        lib.call("eesd_head_argmax_static", x.data_ptr(), None, n, cfg.dim, cfg.vocab_size, w.t["norm"].data_ptr(),
+                 w.t["lm_head"].data_ptr(), cfg.norm_eps, ids.data_ptr(), lib.stream_ptr())
+        return ids
+
+    two, two_static = dm.head_argmax(x), static_head()
+    lib.call("eesd_set_option", lib.OPT_HEAD_TWO_TILES, 0)
+    try:
+        one, one_static = dm.head_argmax(x), static_head()
+    finally:
+        lib.call("eesd_set_option", lib.OPT_HEAD_TWO_TILES, 1)
+    ids, lg = dm.head_argmax(x, logits=True)
+    dm.check()
+    assert torch.equal(two, one)
+    if n <= 128:
+        assert torch.equal(two_static, one_static) and torch.equal(two, two_static)
+    assert torch.equal(two.long(), lg.float().argmax(-1))

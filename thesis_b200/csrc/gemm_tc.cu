@@ -127,7 +127,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x, TcParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  constexpr int kNA = (EPI == EESD_EPI_SWIGLU) ? 2 : 1;
+  // two A tiles per stage: SwiGLU (gate and up rows) and the two-tile head (rows m0 and m0 + 128)
+  constexpr int kNA = (EPI == EESD_EPI_SWIGLU || EPI == EESD_EPI_ARGMAX2_INTERNAL) ? 2 : 1;
   const int b_rows = PAIR ? p.bn / 2 : p.bn;     // token rows this CTA loads per k-block
   const uint32_t b_bytes = (uint32_t)b_rows * kBK * 2;
   const uint32_t stage_bytes = kNA * kATileBytes + b_bytes;
@@ -142,7 +143,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rank = PAIR ? (int)cluster_rank() : 0;          // CTA of the pair (0 issues the MMAs)
   const int tok_tile = PAIR ? blockIdx.y : blockIdx.x;
-  const int out_tile = PAIR ? 2 * blockIdx.z + rank : blockIdx.y;
+  const int out_tile = PAIR ? 2 * blockIdx.z + rank : (EPI == EESD_EPI_ARGMAX2_INTERNAL ? 2 * blockIdx.y : blockIdx.y);
   const int split = PAIR ? 0 : blockIdx.z;
   const int n0 = tok_tile * p.bn, m0 = out_tile * kBM;
   const int kb_begin = split * p.kb_per;
@@ -336,15 +337,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (row_ok) epilogue_cols<EPI, 16>(p, n0 + c, row, v, u);
         }
       }
-    } else {  // ARGMAX: logits rounded to bf16, max over this CTA's 128 rows, then atomicMax
+    } else {  // ARGMAX: logits rounded to bf16, max over this CTA's rows, then atomicMax
       unsigned long long* red = reinterpret_cast<unsigned long long*>(smem);  // stage memory is free now
+      const int row2 = row + kBM;                      // two-tile head: this lane's row of the second tile
+      const bool row2_ok = kNA == 2 && row2 < p.n_out;
       if (epi_warp && ok) {
         for (int c = half * 16; c < p.bn; c += 32) {
-          float v[16];
+          float v[16], v2[16];
           tmem_ld16(lane_base + c, v);
+          if (kNA == 2) tmem_ld16(lane_base + p.bn + c, v2);
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             unsigned long long key = row_ok ? argmax_key(rnd<bf16>(v[j]), (uint32_t)row) : 0ull;
+            if (kNA == 2 && row2_ok) {
+              const unsigned long long k2 = argmax_key(rnd<bf16>(v2[j]), (uint32_t)row2);
+              key = k2 > key ? k2 : key;
+            }
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1) {
               const unsigned long long o = __shfl_xor_sync(0xffffffffu, key, off);
@@ -554,6 +562,7 @@ int g_mma_n_option = 0;   // 0: one MMA spans the whole token tile
 int g_splits_option = 0;  // 0: split count from the weight shape
 int g_stages_option = 0;  // 0: as many stages as the shared-memory budget holds
 int g_pair_option = 1;    // 1: SwiGLU GEMMs whose row tiles pair up run on CTA pairs (cta_group::2)
+int g_head_two_option = 1;  // 1: head launches of up to 256 tokens take two row tiles per CTA
 
 int next_pow2(int v) {
   int p = 32;
@@ -601,7 +610,7 @@ int launch(const TcPlan& pl, const CUtensorMap& map_w, const CUtensorMap& map_x,
   int rc = ensure_smem_attr<EPI, false>(pl.smem);
   if (rc) return rc;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(pl.tok_tiles, pl.out_tiles, pl.splits);
+  cfg.gridDim = dim3(pl.tok_tiles, EPI == EESD_EPI_ARGMAX2_INTERNAL ? (pl.out_tiles + 1) / 2 : pl.out_tiles, pl.splits);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = pl.smem;
   cfg.stream = stream;
@@ -691,6 +700,7 @@ void tc_set_mma_n(int n) { g_mma_n_option = n; }
 void tc_set_splits(int n) { g_splits_option = n; }
 void tc_set_stages(int n) { g_stages_option = n; }
 void tc_set_pair(int n) { g_pair_option = n; }
+void tc_set_head_two_tiles(int n) { g_head_two_option = n; }
 
 TcPlan tc_plan(int n_tok, int n_out, int k, int epi) {
   TcPlan pl{};
@@ -726,7 +736,12 @@ TcPlan tc_plan(int n_tok, int n_out, int k, int epi) {
   if (g_splits_option > 0 && epi != EESD_EPI_ARGMAX_INTERNAL) s = std::min(g_splits_option, kMaxSplits);
   pl.kb_per = (pl.kb_total + s - 1) / s;
   pl.splits = (pl.kb_total + pl.kb_per - 1) / pl.kb_per;
-  const int na = epi == EESD_EPI_SWIGLU ? 2 : 1;
+  // The head (no split) takes two 128-row tiles per CTA where both accumulators fit in TMEM: each
+  // stage then carries 32 KB of weights per barrier round trip instead of 16 KB.  Every logit is
+  // the same k-ordered sum either way and the argmax is order-free, so the choice may depend on
+  // n_tok.
+  pl.argmax2 = epi == EESD_EPI_ARGMAX_INTERNAL && g_head_two_option && pl.bn <= 256;
+  const int na = (epi == EESD_EPI_SWIGLU || pl.argmax2) ? 2 : 1;
   // CTA pairs for unsplit SwiGLU tiles (a whole number of 256-row tiles, one MMA per accumulator);
   // the choice depends on the weight shape and the option only, never on n_tok
   pl.pair = epi == EESD_EPI_SWIGLU && g_pair_option && mma_fixed == 0 && pl.splits == 1 && n_out % (2 * kBM) == 0 &&
@@ -773,7 +788,7 @@ int tc_gemm_launch(int epi, const CUtensorMap& map_w, const void* x, int n_tok, 
   p.kb_per = pl.kb_per;
   p.splits = pl.splits;
   p.stages = pl.stages;
-  p.up_offset = up_offset;
+  p.up_offset = pl.argmax2 ? kBM : up_offset;   // two-tile head: the second A tile is the next 128 rows
   p.tmem_cols = pl.tmem_cols;
   p.a_packed = a_packed;
   p.acc_cols = pl.acc_cols;
@@ -791,7 +806,9 @@ int tc_gemm_launch(int epi, const CUtensorMap& map_w, const void* x, int n_tok, 
     case EESD_EPI_STORE: return launch<EESD_EPI_STORE>(pl, map_w, map_x, p, stream);
     case EESD_EPI_RESIDUAL: return launch<EESD_EPI_RESIDUAL>(pl, map_w, map_x, p, stream);
     case EESD_EPI_SWIGLU: return launch<EESD_EPI_SWIGLU>(pl, map_w, map_x, p, stream);
-    case EESD_EPI_ARGMAX_INTERNAL: return launch<EESD_EPI_ARGMAX_INTERNAL>(pl, map_w, map_x, p, stream);
+    case EESD_EPI_ARGMAX_INTERNAL:
+      return pl.argmax2 ? launch<EESD_EPI_ARGMAX2_INTERNAL>(pl, map_w, map_x, p, stream)
+                        : launch<EESD_EPI_ARGMAX_INTERNAL>(pl, map_w, map_x, p, stream);
     default: return EESD_ERR_ARG;
   }
 }

@@ -6,6 +6,7 @@
 #include <stddef.h>
 
 #define EESD_EPI_ARGMAX_INTERNAL 3   // head: logits rounded to bf16 -> per-token argmax keys
+#define EESD_EPI_ARGMAX2_INTERNAL 4  // the same, two 128-row tiles per CTA (two accumulators)
 
 namespace eesd {
 
@@ -16,6 +17,7 @@ typedef CUresult (*PFN_encodeTiled_t)(CUtensorMap*, CUtensorMapDataType, cuuint3
 struct TcPlan {
   int tok_tiles, out_tiles, bn, b_boxes, mma_n, kb_total, kb_per, splits, stages, acc_cols, tmem_cols;
   int pair;               // 1: CTA pairs (cta_group::2), grid (2, tok_tiles, out_tiles / 2)
+  int argmax2;            // head: two row tiles per CTA, grid (tok_tiles, ceil(out_tiles / 2), 1)
   size_t smem;
   size_t partial_bytes;   // split-K scratch the launch needs (0 without split)
 };
@@ -34,6 +36,7 @@ void tc_set_mma_n(int n);
 void tc_set_splits(int n);
 void tc_set_stages(int n);
 void tc_set_pair(int n);
+void tc_set_head_two_tiles(int n);
 // a_packed = 1: map_w is a tile-packed weight map (encode_packed_map), else a row-major 2-D map
 int tc_gemm_launch(int epi, const CUtensorMap& map_w, const void* x, int n_tok, int n_out, int k, int up_offset,
                    const void* residual, int ld_res, void* y, int ld_y, unsigned long long* keys, int* status,

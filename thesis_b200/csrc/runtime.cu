@@ -604,6 +604,11 @@ int eesd_set_option(int option, int value) {
     tc_set_pair(value);
     return EESD_OK;
   }
+  if (option == 5) {   // LM head: two row tiles per CTA up to 256 tokens: 1 = on (default), 0 = off
+    if (value < 0 || value > 1) return fail(EESD_ERR_ARG, "head two tiles %d", value);
+    tc_set_head_two_tiles(value);
+    return EESD_OK;
+  }
   return fail(EESD_ERR_ARG, "unknown option %d", option);
 }
 
