@@ -1,13 +1,15 @@
 """Small, self-contained profiling workload for single-kernel captures (ncu) of the hot path.
 
-    python -m thesis_b200.profile_layer [--iters N] [--layers 2] [--ctx 300 700]
+    python -m thesis_b200.profile_layer [--iters N] [--layers 2] [--ctx 300 700] [--prefill]
 
 Builds a LayerSkip-Llama3-8B-shaped model with only ``--layers`` layers (random bf16 weights,
 about 2 GB on the device with the KV cache), fills the KV cache with random values, and runs a
 verify-shaped packed call (64 blocks of 5 tokens), a draft-shaped call (64 blocks of 1 token) and
 the exit head on both, ``--iters`` times, then the same again under per-launch CUDA events and
 prints the average time of every (kernel kind, token count).  Inputs are larger than L2 (436 MB
-of weights per layer, ~130 MB of KV per attention launch).
+of weights per layer, ~130 MB of KV per attention launch).  ``--prefill`` adds a prefill-shaped
+call (4 requests x 512 prompt tokens from position 0), which runs the separate RoPE/KV-append
+kernel.
 """
 
 from __future__ import annotations
@@ -27,10 +29,11 @@ def main(argv=None) -> None:
     ap.add_argument("--iters", type=int, default=1)
     ap.add_argument("--layers", type=int, default=2)
     ap.add_argument("--ctx", type=int, nargs=2, default=(300, 700))
+    ap.add_argument("--prefill", action="store_true")
     args = ap.parse_args(argv)
     cfg = replace(preset("llama3-8b"), n_layers=args.layers)
     w = ModelWeights.synthetic(cfg, seed=0, dtype=torch.bfloat16, device="cuda")
-    dm = DeviceModel(w, max_batch=64, max_seq=args.ctx[1] + 64, max_tokens=512)
+    dm = DeviceModel(w, max_batch=64, max_seq=max(args.ctx[1], 512) + 64, max_tokens=2048 if args.prefill else 512)
     dm.k_cache.normal_(0, 0.5)
     dm.v_cache.normal_(0, 0.5)
     rng = np.random.default_rng(0)
@@ -41,11 +44,17 @@ def main(argv=None) -> None:
     xd = torch.randn(320, cfg.dim, device="cuda", generator=g).bfloat16()
     xs = torch.randn(64, cfg.dim, device="cuda", generator=g).bfloat16()
 
+    if args.prefill:
+        pre = dm.upload(dm.pack([(r, 0, 512) for r in range(60, 64)]))
+        xp = torch.randn(2048, cfg.dim, device="cuda", generator=g).bfloat16()
+
     def once():
         dm.forward_layers(xd.clone(), deep, 0, cfg.n_layers)
         dm.forward_layers(xs.clone(), shal, 0, cfg.n_layers)
         dm.head_argmax(xs)
         dm.head_argmax(xd)
+        if args.prefill:
+            dm.forward_layers(xp.clone(), pre, 0, cfg.n_layers)
 
     for _ in range(args.iters):
         once()
