@@ -181,15 +181,30 @@ def cpu_baseline(tokens_per_round: float, n_samples: int = 1) -> dict:
                        f"{n_samples} sample(s)")}
 
 
+def _all_host_threads():
+    """Let the CPU sample's BLAS / OpenMP pools use every core this process may run on (a
+    launcher such as torchrun sets OMP_NUM_THREADS=1 for each rank)."""
+    import contextlib
+
+    try:
+        import numpy  # noqa: F401 - its BLAS must be loaded for the limit to reach it
+        from threadpoolctl import threadpool_limits
+
+        return threadpool_limits(limits=len(os.sched_getaffinity(0)))
+    except Exception:
+        return contextlib.nullcontext()
+
+
 def run_reference(args) -> None:
     if int(os.environ.get("RANK", "0")) != 0:
         return
     tpr = args.tokens_per_round
-    for _ in range(args.warmup):
-        cpu_baseline(tpr, 1)
-    t0 = time.perf_counter()
-    cb = cpu_baseline(tpr, max(args.steps, 1))
-    wall = time.perf_counter() - t0
+    with _all_host_threads():
+        for _ in range(args.warmup):
+            cpu_baseline(tpr, 1)
+        t0 = time.perf_counter()
+        cb = cpu_baseline(tpr, max(args.steps, 1))
+        wall = time.perf_counter() - t0
     line = {"metric": METRIC, "value": cb["value"], "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1000 * wall / max(args.steps, 1), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
@@ -381,7 +396,10 @@ def run_ours(args) -> None:
 
     if rank == 0:
         acc_tokens_per_round = committed / max(args.steps, 1)
-        cb = None if args.no_cpu else cpu_baseline(acc_tokens_per_round, 1)
+        cb = None
+        if not args.no_cpu and world == 1:         # the CPU baseline is taken on 1 GPU runs only
+            with _all_host_threads():
+                cb = cpu_baseline(acc_tokens_per_round, 1)
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "rank_ms_per_step": rank_ms,
