@@ -15,8 +15,11 @@ tokens (NCCL all_gather) inside the timed region.  ``--strong`` shards the 64 re
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--strong]
 
-``--impl reference`` times the reference algorithm's CPU implementation (the numpy port under
-``oracle/``, fp32 as the reference runs on CPU) on a bounded sample of the same workload.
+``--impl reference`` times the reference's own CPU implementation of the path - its
+``common/model.py`` + ``solutions/packed.py``, installed unmodified under ``baseline/_ref`` (see
+``baseline/install_reference.sh``), fp32 as the reference runs on CPU (common/cli.py:22-24) - on a
+bounded sample of the same workload; without that install it falls back to the numpy port of the
+same algorithm under ``oracle/`` and says so (``kind``).
 """
 
 from __future__ import annotations
@@ -36,6 +39,13 @@ sys.path.insert(0, str(ROOT))
 
 B_PER_GPU, EXIT, GAMMA, MAX_NEW = 64, 8, 4, 512
 PROMPT_LEN = (128, 512)
+# Tokens committed per draft/verify round by the B200 engine on this workload (64 requests, default
+# --warmup 3 --steps 20), as measured by this script's own arm.  The reference arm composes a round
+# from timed pieces and divides these tokens by it: the reference decodes the same prompts with
+# the same greedy draft/verify rule, so a round of it commits the same tokens (its fp32 arithmetic
+# can move an acceptance by a near-tie; the arm states the value it used).
+TOKENS_PER_ROUND = 157.6
+REF_DIR = ROOT / "baseline" / "_ref"
 METRIC = "generated tokens/s/GPU, LayerSkip-8B bf16 B=64 E=8 k=4; verify-step p50 ms"
 WORKLOAD = ("C3: LayerSkip-Llama3-8B-shaped bf16 (32 layers, dim 4096, 32q/8kv heads of 128, SwiGLU 14336, "
             "vocab 128256, untied), random init seed 0, residual outputs of layers >= 8 scaled by 0.1; "
@@ -181,6 +191,95 @@ def cpu_baseline(tokens_per_round: float, n_samples: int = 1) -> dict:
                        f"{n_samples} sample(s)")}
 
 
+def reference_installed() -> bool:
+    return (REF_DIR / "common" / "model.py").exists() and (REF_DIR / "solutions" / "packed.py").exists()
+
+
+def cpu_reference_sample(tokens_per_round: float, n_samples: int = 1, warmup: int = 1) -> dict:
+    """The reference's own path on the host cores: ``common/model.py`` + ``solutions/packed.py``
+    from the unmodified install under baseline/_ref, fp32, torch with every host thread.  Bounded
+    sample at the C3 shapes: ``build_packed`` + ``packed_layer`` on one shallow layer (64 blocks of
+    1 token) and one deep layer (64 blocks of 5 tokens) at the workload's mean context, and the
+    shared head on 64 and 320 rows (1/8 of the vocabulary, scaled x8: the head GEMM is linear in
+    it); a round = gamma + 1 shallow packings and passes of 8 layers, gamma draft heads, one deep
+    packing and 24 deep layers, one verify head."""
+    import torch
+
+    from thesis_b200.config import preset
+
+    if str(REF_DIR) not in sys.path:
+        sys.path.insert(0, str(REF_DIR))
+    from common.model import LayerSkipLlama, LayerWeights, ModelConfig
+    from solutions.packed import Block, build_packed, packed_layer
+
+    torch.set_num_threads(len(os.sched_getaffinity(0)))
+    c = preset("llama3-8b")
+    vshare = 8
+    B = B_PER_GPU
+    ctx = (PROMPT_LEN[0] + PROMPT_LEN[1]) // 2 + MAX_NEW // 2          # mean context over a run
+    max_seq = ctx + GAMMA + 64
+    rc = ModelConfig(vocab_size=c.vocab_size // vshare, dim=c.dim, n_layers=1, n_heads=c.n_heads,
+                     n_kv_heads=c.n_kv_heads, head_dim=c.head_dim, intermediate_size=c.intermediate_size,
+                     norm_eps=c.norm_eps, rope_theta=c.rope_theta, max_position_embeddings=max_seq,
+                     tie_word_embeddings=False)
+    g = torch.Generator().manual_seed(0)
+
+    def mat(r, k):
+        return torch.randn(r, k, generator=g) * 0.02
+
+    qkv_rows = (c.n_heads + 2 * c.n_kv_heads) * c.head_dim
+    lw = LayerWeights(wqkv=mat(qkv_rows, c.dim), wo=mat(c.dim, c.n_heads * c.head_dim),
+                      w13=mat(2 * c.intermediate_size, c.dim), w2=mat(c.dim, c.intermediate_size),
+                      attn_norm=torch.ones(c.dim), ffn_norm=torch.ones(c.dim))
+    m = LayerSkipLlama(rc, mat(rc.vocab_size, c.dim), [lw], torch.ones(c.dim), mat(rc.vocab_size, c.dim), "cpu",
+                       torch.float32, max_seq)
+    m.allocate_cache(B, max_seq)
+    m.cache.k[0].normal_(0.0, 0.1, generator=g)
+    m.cache.v[0].normal_(0.0, 0.1, generator=g)
+    x_sh = torch.randn(B, c.dim, generator=g)
+    x_dp = torch.randn(B * (GAMMA + 1), c.dim, generator=g)
+    sh_blocks = [Block(r, ctx, 1) for r in range(B)]
+    dp_blocks = [Block(r, ctx - GAMMA, GAMMA + 1) for r in range(B)]
+
+    def step(x, blocks):
+        t0 = time.perf_counter()
+        pb = build_packed(m, blocks, "exact")
+        t1 = time.perf_counter()
+        packed_layer(m, 0, x, pb)
+        t2 = time.perf_counter()
+        m.head(x)
+        t3 = time.perf_counter()
+        return t1 - t0, t2 - t1, (t3 - t2) * vshare
+
+    samples = []
+    with torch.inference_mode():
+        for i in range(warmup + n_samples):
+            p_sh, l_sh, h_sh = step(x_sh, sh_blocks)
+            p_dp, l_dp, h_dp = step(x_dp, dp_blocks)
+            rnd = (GAMMA + 1) * (p_sh + EXIT * l_sh) + GAMMA * h_sh + p_dp + (c.n_layers - EXIT) * l_dp + h_dp
+            if i >= warmup:
+                samples.append(tokens_per_round / rnd)
+    return {"value": float(statistics.median(samples)), "unit": "tokens/s", "cores": int(torch.get_num_threads()),
+            "kind": "reference",
+            "sample": (f"the reference's common/model.py + solutions/packed.py (baseline/_ref, unmodified), fp32 on "
+                       f"{torch.get_num_threads()} torch threads, C3 shapes: build_packed + packed_layer for 1 shallow "
+                       f"layer (64x1 tok) and 1 deep layer (64x5 tok) at context {ctx}, head on 64 and 320 rows "
+                       f"(1/{vshare} of the vocab, x{vshare}), composed into a round (5 x (pack + 8 shallow layers) + "
+                       f"4 heads + pack + 24 deep layers + head); {tokens_per_round:.1f} tokens/round; median of "
+                       f"{n_samples} sample(s) after {warmup} warm-up")}
+
+
+def cpu_sample(tokens_per_round: float, n_samples: int, warmup: int) -> dict:
+    """The reference's own CPU path when it is installed, else the numpy port of it."""
+    if reference_installed():
+        return cpu_reference_sample(tokens_per_round, n_samples, warmup)
+    for _ in range(warmup):
+        cpu_baseline(tokens_per_round, 1)
+    cb = cpu_baseline(tokens_per_round, n_samples)
+    cb["sample"] += " (baseline/_ref absent: numpy port)"
+    return cb
+
+
 def _all_host_threads():
     """Let the CPU sample's BLAS / OpenMP pools use every core this process may run on (a
     launcher such as torchrun sets OMP_NUM_THREADS=1 for each rank)."""
@@ -200,17 +299,15 @@ def run_reference(args) -> None:
         return
     tpr = args.tokens_per_round
     with _all_host_threads():
-        for _ in range(args.warmup):
-            cpu_baseline(tpr, 1)
         t0 = time.perf_counter()
-        cb = cpu_baseline(tpr, max(args.steps, 1))
+        cb = cpu_sample(tpr, max(args.steps, 1), args.warmup)
         wall = time.perf_counter() - t0
     line = {"metric": METRIC, "value": cb["value"], "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1000 * wall / max(args.steps, 1), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": WORKLOAD + " (CPU sample)", "global_batch": B_PER_GPU, "seq_len": MAX_NEW,
                        "parallelism": "host cores"},
-            "impl": "reference", "cpu_baseline": cb,
+            "impl": "reference", "cpu_baseline": cb, "tokens_per_round": tpr,
             "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -398,8 +495,8 @@ def run_ours(args) -> None:
         acc_tokens_per_round = committed / max(args.steps, 1)
         cb = None
         if not args.no_cpu and world == 1:         # the CPU baseline is taken on 1 GPU runs only
-            with _all_host_threads():
-                cb = cpu_baseline(acc_tokens_per_round, 1)
+            with _all_host_threads():               # same sample count and warm-up as the reference arm
+                cb = cpu_sample(acc_tokens_per_round, args.steps, args.warmup)
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "rank_ms_per_step": rank_ms,
@@ -420,6 +517,8 @@ def run_ours(args) -> None:
             "gpu_launches": int(launches),
             "roofline": {"bound": "tensor" if tensor_bound else "hbm", "achieved": achieved, "peak": peak,
                          "unit": unit, "frac": achieved / peak, "traffic": recorded_traffic(f"{dk}@{dn}"),
+                         "traffic_source": "dram read+write bytes per launch from the ncu capture recorded in "
+                                           "profiles/ncu_traffic.txt (an earlier run of the same kernel, not this one)",
                          "kernel": f"{dk}@{dn} tokens",
                          "launches": dcount, "avg_ms": avg_s * 1000, "peak_source": pk["source"],
                          "timing": f"per-launch CUDA events over {args.profile_rounds} profiled rounds after the timed region"},
@@ -452,8 +551,9 @@ def main():
     ap.add_argument("--strong", action="store_true",
                     help="strong scaling: the 64 requests of the 1-GPU run sharded over the GPUs (default: 64 per GPU)")
     ap.add_argument("--profile-rounds", type=int, default=3, help="profiled rounds after the timed region")
-    ap.add_argument("--tokens-per-round", type=float, default=3.5 * B_PER_GPU,
-                    help="reference arm: tokens committed per round (the GPU engine's measured value)")
+    ap.add_argument("--tokens-per-round", type=float, default=TOKENS_PER_ROUND,
+                    help="reference arm: tokens committed per round (default: the B200 engine's measured value "
+                         "on this workload)")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")

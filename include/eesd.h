@@ -189,6 +189,30 @@ int eesd_round_advance(const int32_t* act, int n, const int32_t* acc, int32_t* p
 int eesd_rmsnorm(int dtype, const void* x, const int32_t* rows, const void* w, void* y, int n, int dim, float eps,
                  void* stream);
 
+/* Varlen GQA attention of one packed batch over ONE layer's KV cache.  solutions/packed.py:142-166
+ * (`_attend`: per-bucket SDPA over [b, Hkv, G T, D] queries with a bool mask) without buckets or
+ * masks: query (token t of block b, head h) attends to positions <= pos0_b + t of row row_b.
+ * qkv [n_tokens, (Hq + 2 Hkv) D] is the fused projection output (q heads first, then k, then v);
+ * k_cache / v_cache [max_batch, Hkv, max_seq, D]; out [n_tokens, Hq D].  The batch's `items` tile
+ * every block into work items of eesd_attn_item_tokens() tokens (tok_pos / tok_row are unused).
+ * append = 0: q is used as given (already rotated) and the cache already holds this call's keys.
+ * append = 1 (bf16, every block one item, no two blocks on the same cache row): the kernel applies
+ * RoPE (rope_cos / rope_sin [max_seq, D] fp32, solutions/packed.py:176-177) to q and k and writes k,
+ * v at (row, position) first (solutions/packed.py:180-181).  Each work item appends only its own
+ * block's keys, so a row's blocks must come in separate calls (or use eesd_rope_kv_append first).  An item whose block lies outside the batch or whose positions lie
+ * outside its row sets a bit in *status (device int32, nullable) and is skipped. */
+int eesd_attn_varlen_gqa(int dtype, const void* qkv, int n_heads, int n_kv_heads, int head_dim, void* k_cache,
+                         void* v_cache, int max_batch, int max_seq, const EesdBatch* batch, int append,
+                         const float* rope_cos, const float* rope_sin, void* out, int32_t* status, void* stream);
+
+/* RoPE of q and k and the in-place KV append of a packed batch (common/model.py:143-150 apply_rope,
+ * solutions/packed.py:176-181): q rotated in place in qkv, rotated k and v written to
+ * k_cache / v_cache [max_batch, Hkv, max_seq, D] at (tok_row[t], tok_pos[t]).  A token whose row or
+ * position is out of range sets a bit in *status (nullable) and is skipped. */
+int eesd_rope_kv_append(int dtype, void* qkv, const int32_t* tok_pos, const int32_t* tok_row, int n_tok, int n_heads,
+                        int n_kv_heads, int head_dim, const float* rope_cos, const float* rope_sin, void* k_cache,
+                        void* v_cache, int max_batch, int max_seq, int32_t* status, void* stream);
+
 /* y[n_tok, n_out] = epilogue(x[n_tok, k] @ w[n_out(+up), k]^T).  workspace: see
  * eesd_gemm_workspace_bytes (split-K partials and tile counters; zeroed by this call). */
 size_t eesd_gemm_workspace_bytes(int n_tok, int n_out, int k, int epilogue);
@@ -209,21 +233,30 @@ int eesd_gemm(int dtype, int epilogue, const void* x, const void* w, const void*
 #define EESD_OPT_STAGES 3
 #define EESD_OPT_PAIR 4
 #define EESD_OPT_HEAD_TWO_TILES 5
+/* EESD_OPT_SPIN_LIMIT (tests of the failure path): poll limit of the pipeline waits of the GEMM and
+ * attention kernels launched afterwards; -1 restores the default (2^24 polls), 0 makes every such
+ * wait give up at once.  A wait that gives up sets a timeout bit in the device status word, the
+ * kernel lets the copies and MMAs it already issued land, and returns. */
+#define EESD_OPT_SPIN_LIMIT 6
 int eesd_set_option(int option, int value);
 
 /* Exit head that allocates nothing, for callers that cannot call cudaMalloc (a serving
  * runtime whose allocator is locked on its decode path, code inside a foreign stream capture, a
  * plug-in that only receives input/output pointers).  No counterpart in the reference: it is the
  * same computation as eesd_head_argmax (final RMSNorm with norm_w, LM head, greedy argmax of rows
- * `rows` (nullable = 0..n-1) of x [*, dim] bf16 -> out_ids [n] int32) without a model handle or
- * workspace.  Its scratch is a fixed 2 MiB + 1280 B __device__ array inside the library, held by
- * every GPU that loads the library until exit.  Limits: bf16, 1 <= n <= 128, dim a multiple of
- * 64 up to 8192; larger sizes return EESD_ERR_ARG with a message.  The first call on a device
- * resolves the array's device address (cudaGetSymbolAddress) and should come before any stream
- * capture.  All calls share the array: calls that overlap on the GPU race and must be serialised
- * by the caller. */
-int eesd_head_argmax_static(const void* x, const int32_t* rows, int n, int dim, int vocab, const void* norm_w,
-                            const void* lm_head, float eps, int32_t* out_ids, void* stream);
+ * `rows` (nullable = 0..n-1) of x [x_rows, dim] bf16 -> out_ids [n] int32) without a model handle
+ * or workspace.  Its scratch is a fixed 2 MiB + 1280 B __device__ array inside the library, held
+ * by every GPU that loads the library until exit.  Limits: bf16, 1 <= n <= 128, dim a multiple of
+ * 64 up to 8192; larger sizes return EESD_ERR_ARG with a message.  `stream` must belong to the
+ * current device.  The first call on a device resolves the array's device address
+ * (cudaGetSymbolAddress) and should come before any stream capture.  All calls share the array:
+ * calls that overlap on the GPU race and must be serialised by the caller.
+ * Device-side errors: a row index outside [0, x_rows) or a bounded wait that gave up makes every
+ * out_id -1, and the call's status bits (0 = none) are written to *status_out (device int32,
+ * nullable), both on the stream. */
+int eesd_head_argmax_static(const void* x, int x_rows, const int32_t* rows, int n, int dim, int vocab,
+                            const void* norm_w, const void* lm_head, float eps, int32_t* out_ids,
+                            int32_t* status_out, void* stream);
 
 /* Device status word helpers for the primitive kernels (a caller-owned int32). */
 int eesd_status_read(const int32_t* status, int* bits_out, void* stream);

@@ -247,8 +247,8 @@ def test_head_two_row_tiles_per_cta(cuda_dev, n):
         ids = torch.full((n,), -1, dtype=torch.int32, device=cuda_dev)
         if n > 128:
             return None
-        lib.call("eesd_head_argmax_static", x.data_ptr(), None, n, cfg.dim, cfg.vocab_size, w.t["norm"].data_ptr(),
-                 w.t["lm_head"].data_ptr(), cfg.norm_eps, ids.data_ptr(), lib.stream_ptr())
+        lib.call("eesd_head_argmax_static", x.data_ptr(), n, None, n, cfg.dim, cfg.vocab_size, w.t["norm"].data_ptr(),
+                 w.t["lm_head"].data_ptr(), cfg.norm_eps, ids.data_ptr(), None, lib.stream_ptr())
         return ids
 
     two, two_static = dm.head_argmax(x), static_head()

@@ -67,3 +67,19 @@ def test_greedy_tokens_match_reference_fp32(name):
 
 def test_argmax_ties_take_the_lowest_index():
     assert int(argmax_first(np.array([1.0, 3.0, 3.0, 2.0]))) == 1
+
+
+def test_oracle_at_benchmark_config1_matches_reference():
+    """BASELINE configuration 1 at full size (Llama3.2-1B shape, fp32): the oracle's prefill, exit
+    and final logits match the reference's within 1e-4 (stored columns of the 128256-entry rows)."""
+    from goldens import sparse_rel_err
+
+    g = Golden("c1_fp32")
+    m = _oracle(g)
+    rows = [m.prefill(p, slot=i) for i, p in enumerate(g.prompts())]
+    assert sparse_rel_err(g, "prefill_logits", np.stack(rows)) < TOL["fp32"]
+    blocks = [tuple(map(int, b)) for b in g["packed_blocks"]]
+    E = g.meta["exit_layer"]
+    h, cap = m.packed_layers(m.embed(g["packed_ids"]), blocks, 0, m.cfg.n_layers, capture=(E,))
+    assert sparse_rel_err(g, "packed_exit_logits", m.head(cap[E])) < TOL["fp32"]
+    assert sparse_rel_err(g, "packed_final_logits", m.head(h)) < TOL["fp32"]

@@ -29,6 +29,12 @@ enum : int {
 
 constexpr uint32_t kSpinLimit = 1u << 24;
 
+// Poll limit of the pipeline waits of the next launches (host side; kernels receive it as a
+// parameter).  kSpinLimit unless a test lowered it with eesd_set_option(EESD_OPT_SPIN_LIMIT): a
+// limit of 0 makes every pipeline wait give up at once, which exercises the timeout path.  Waits
+// that drain copies or MMAs already in flight always use kSpinLimit.
+uint32_t spin_limit();
+
 __device__ __forceinline__ float to_f(float x) { return x; }
 __device__ __forceinline__ float to_f(bf16 x) { return __bfloat162float(x); }
 template <typename T> __device__ __forceinline__ T from_f(float x);
@@ -62,13 +68,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait.  Returns false (and leaves the caller to unwind) when the limit is hit or
-// another role of the CTA has already aborted.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+// Bounded wait.  Returns false (and leaves the caller to unwind) when `limit` polls did not see
+// the phase complete or another role of the CTA has already aborted.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                          uint32_t limit = kSpinLimit) {
+  for (uint32_t i = 0; i < limit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 255u) == 255u && *abort_flag) return false;
   }
+  return false;
+}
+// Drain wait after an abort: the phase `parity` of `bar` completes once copies or MMAs already in
+// flight land; bounded by kSpinLimit and blind to the abort flag.
+__device__ __forceinline__ bool mbar_drain(uint32_t bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
   return false;
 }
 

@@ -65,6 +65,7 @@ struct alignas(8) TcParams {
   unsigned long long* keys;  // argmax keys [n_tok]
   float4* partials;          // split-K: [tile][split][acc_cols / 4][128] fp32 partial tiles
   int* status;
+  uint32_t spin;             // poll limit of the pipeline waits (spin_limit())
 };
 
 // named barrier of the 256 epilogue threads (bar.sync counts whole warps: converge first)
@@ -137,7 +138,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty = bars + p.stages;
   uint64_t* accb = bars + 2 * p.stages;
   uint64_t* epib = accb + 1;                 // split-K: staged partials / residual landed
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accb + 2);
+  uint64_t* drainb = accb + 2;               // after an abort: the MMAs already issued completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accb + 3);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -157,6 +159,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(smem_u32(accb), 1);
     mbar_init(smem_u32(epib), 1);
+    mbar_init(smem_u32(drainb), 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -179,6 +182,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (PAIR) cluster_sync();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // what is in flight if the CTA aborts: k-blocks whose loads the producer issued, MMAs issued and
+  // whether their completion was committed to the accumulator barrier (producer / issuer lanes)
+  int loads_issued = 0;
+  bool mma_issued = false, mma_committed = false;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -229,12 +236,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       pdl_wait();
       for (int i = 0; i < pre; ++i) load_b(i, smem_u32(smem + (size_t)i * stage_bytes), fbar(i));
+      loads_issued = pre;
       const int stages = p.stages;
       const uint32_t smem0 = smem_u32(smem), empty0 = smem_u32(empty);
       int s = pre % stages, ph = (pre / stages) & 1;   // ring slot of k-block i and its fill parity
       for (int i = pre; i < nkb; ++i) {
         // slot s was last filled for k-block i - stages: wait for the MMAs that read it
-        if (!mbar_wait(empty0 + 8u * s, ph ^ 1, abort_flag)) {
+        if (!mbar_wait(empty0 + 8u * s, ph ^ 1, abort_flag, p.spin)) {
           set_status(p.status, kStatusTimeoutProducer);
           *abort_flag = 1;
           break;
@@ -244,6 +252,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t fb = fbar(s);
         load_a(i, st, fb);
         load_b(i, st, fb);
+        loads_issued = i + 1;
         if (++s == stages) { s = 0; ph ^= 1; }
       }
     }
@@ -262,13 +271,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       int s = 0, ph = 0;
       for (int i = 0; i < nkb; ++i) {
-        if (!mbar_wait(full0 + 8u * s, ph, abort_flag)) {
+        if (!mbar_wait(full0 + 8u * s, ph, abort_flag, p.spin)) {
           set_status(p.status, kStatusTimeoutMma);
           *abort_flag = 1;
           ok = false;
           break;
         }
         tc_fence_after();
+        mma_issued = true;
         const uint64_t da = desc_hi | (uint64_t)(a_lo0 + (uint32_t)s * stage_lo);
         const uint64_t db = da + (uint64_t)(kNA * (kATileBytes >> 4));
 #pragma unroll
@@ -301,6 +311,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else {
           tc_commit(smem_u32(accb));
         }
+        mma_committed = true;
       }
     }
     __syncwarp();
@@ -319,7 +330,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   bool copies_issued = false;   // split-K staging: this thread issued bulk copies into epib
   if (epi_warp) {
     pdl_wait();
-    ok = mbar_wait(smem_u32(accb), 0, abort_flag);
+    ok = mbar_wait(smem_u32(accb), 0, abort_flag, p.spin);
     if (!ok) {
       set_status(p.status, kStatusTimeoutEpilogue);
       *abort_flag = 1;
@@ -416,7 +427,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool issuer_ok = true;
     if (staged && warp == 0 && lane == 0) {
       // the stage memory is free once every MMA has completed
-      issuer_ok = mbar_wait(smem_u32(accb), 0, abort_flag);
+      issuer_ok = mbar_wait(smem_u32(accb), 0, abort_flag, p.spin);
       if (issuer_ok) {
         copies_issued = true;
         mbar_arrive_expect_tx(smem_u32(epib), part_stage + res_bytes);
@@ -441,7 +452,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     if (epi_warp && ok && staged) {
-      if (!mbar_wait(smem_u32(epib), 0, abort_flag)) {
+      if (!mbar_wait(smem_u32(epib), 0, abort_flag, p.spin)) {
         set_status(p.status, kStatusTimeoutEpilogue);
         *abort_flag = 1;
       } else {
@@ -537,12 +548,39 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (copies_issued && *abort_flag) {
     // the bulk copies this CTA issued land before it exits, even if its epilogue gave up
-    for (uint32_t i = 0; i < kSpinLimit && !mbar_try_wait(smem_u32(epib), 0); ++i) {
-    }
+    mbar_drain(smem_u32(epib), 0);
   }
   tc_fence_before();
   __syncwarp();
   __syncthreads();
+  // Every role has finished, so the abort flag is final.  After an abort, loads and MMAs may still
+  // be in flight: the CTA leaves (and frees its TMEM) only once they have landed.  Each ring slot has
+  // at most one load phase outstanding (the producer refills a slot only after its MMAs freed it), so
+  // waiting for the phase of the last k-block loaded into each slot drains them all.  A CTA pair's
+  // loads complete on the even CTA's barriers, which the even CTA drains before the closing cluster
+  // barrier releases the odd one.
+  if (*abort_flag) {
+    if (warp == 0 && lane == 0 && (!PAIR || rank == 0)) {
+      for (int slot = 0; slot < p.stages && slot < loads_issued; ++slot) {
+        const int last = slot + (loads_issued - 1 - slot) / p.stages * p.stages;
+        mbar_drain(smem_u32(&full[slot]), (uint32_t)(last / p.stages) & 1u);
+      }
+    }
+    if (warp == 1 && lane == 0 && mma_issued) {
+      if (mma_committed) {
+        mbar_drain(smem_u32(accb), 0);
+      } else {
+        if (PAIR)
+          tc_commit_pair(smem_u32(drainb));
+        else
+          tc_commit(smem_u32(drainb));
+        mbar_drain(smem_u32(drainb), 0);
+      }
+    }
+    tc_fence_before();
+    __syncwarp();
+    __syncthreads();
+  }
   // a CTA of a pair leaves only when both are done: the even CTA's MMAs and commits reach the odd
   // CTA's TMEM and barriers, the odd CTA's loads reach the even CTA's barriers
   if (PAIR) cluster_sync();
@@ -802,6 +840,7 @@ int tc_gemm_launch(int epi, const CUtensorMap& map_w, const void* x, int n_tok, 
   p.ld_y = ld_y;
   p.keys = keys;
   p.status = status;
+  p.spin = spin_limit();
   switch (epi) {
     case EESD_EPI_STORE: return launch<EESD_EPI_STORE>(pl, map_w, map_x, p, stream);
     case EESD_EPI_RESIDUAL: return launch<EESD_EPI_RESIDUAL>(pl, map_w, map_x, p, stream);

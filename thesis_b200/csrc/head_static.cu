@@ -12,6 +12,10 @@
 // The caller still passes the inputs (hidden states, final-norm weight, LM head) and the output
 // (token ids).  All calls share the one array: calls that overlap on the GPU (different streams,
 // or different host threads) race on it and must be serialised by the caller.
+//
+// Errors found on the device (a row index outside x, a bounded wait of the GEMM that gave up) are
+// not silent: every id of the call becomes -1 and the call's status bits go to status_out, both
+// written on the stream, so the caller reads them with its own synchronisation.
 #include <mutex>
 
 #include "common.cuh"
@@ -42,11 +46,15 @@ void* g_scratch_dev[kMaxDevices] = {};
 
 using namespace eesd;
 
-extern "C" int eesd_head_argmax_static(const void* x, const int32_t* rows, int n, int dim, int vocab,
+extern "C" int eesd_head_argmax_static(const void* x, int x_rows, const int32_t* rows, int n, int dim, int vocab,
                                        const void* norm_w, const void* lm_head, float eps, int32_t* out_ids,
-                                       void* stream) {
+                                       int32_t* status_out, void* stream) {
   if (!x || !norm_w || !lm_head || !out_ids) {
     set_last_error("head_argmax_static: null pointer argument");
+    return EESD_ERR_ARG;
+  }
+  if (x_rows < 1 || (!rows && x_rows < n)) {
+    set_last_error("head_argmax_static: x_rows must be >= 1, and >= n without a row list");
     return EESD_ERR_ARG;
   }
   if (n < 1 || n > kMaxRows) {
@@ -66,6 +74,13 @@ extern "C" int eesd_head_argmax_static(const void* x, const int32_t* rows, int n
     set_last_error("head_argmax_static: no usable current CUDA device");
     return EESD_ERR_CUDA;
   }
+  // the scratch address below belongs to the current device: the stream must be one of its streams
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int stream_dev = -1;
+  if (cudaStreamGetDevice(s, &stream_dev) != cudaSuccess || stream_dev != dev) {
+    set_last_error("head_argmax_static: the stream does not belong to the current CUDA device");
+    return EESD_ERR_ARG;
+  }
   void* base = nullptr;
   {
     std::lock_guard<std::mutex> lock(g_mu);
@@ -80,7 +95,6 @@ extern "C" int eesd_head_argmax_static(const void* x, const int32_t* rows, int n
     }
     base = g_scratch_dev[dev];
   }
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint8_t* b = static_cast<uint8_t*>(base);
   int* status = reinterpret_cast<int*>(b + kStatusOff);
   unsigned long long* keys = reinterpret_cast<unsigned long long*>(b + kKeysOff);
@@ -90,7 +104,7 @@ extern "C" int eesd_head_argmax_static(const void* x, const int32_t* rows, int n
     set_last_error("head_argmax_static: scratch reset failed");
     return EESD_ERR_CUDA;
   }
-  int rc = launch_rmsnorm(EESD_BF16, x, rows, norm_w, xn, n, dim, eps, s);
+  int rc = launch_rmsnorm(EESD_BF16, x, rows, norm_w, xn, n, dim, eps, s, x_rows, status);
   if (rc) {
     set_last_error("head_argmax_static: rmsnorm launch failed");
     return rc;
@@ -103,7 +117,7 @@ extern "C" int eesd_head_argmax_static(const void* x, const int32_t* rows, int n
   }
   rc = tc_gemm_launch(EESD_EPI_ARGMAX_INTERNAL, map, xn, n, vocab, dim, 0, nullptr, 0, nullptr, 0, keys, status, s, 0,
                       TcScratch{});  // the head is never split: no partial-tile scratch
-  if (!rc) rc = launch_keys_to_ids(keys, out_ids, n, s);
+  if (!rc) rc = launch_keys_to_ids(keys, out_ids, n, s, status, status_out);
   if (rc) set_last_error("head_argmax_static: head GEMM / argmax launch failed");
   return rc;
 }

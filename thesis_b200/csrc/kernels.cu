@@ -33,14 +33,21 @@ __device__ __forceinline__ float warp_max(float v) {
 // (fixed per-thread chunks, then a fixed tree), so a row's result never depends on which other
 // rows share the launch.  bf16 rows of dim <= 8 * 256 * kVec are held in registers between the
 // two passes (16-byte loads).
+// With a row list, a source row outside [0, n_src) sets kStatusBadIndex and its output row is zeroed.
 template <typename T>
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const T* __restrict__ x, const int32_t* __restrict__ rows,
-                                                      const T* __restrict__ w, T* __restrict__ y, int dim, float eps) {
+                                                      const T* __restrict__ w, T* __restrict__ y, int dim, float eps,
+                                                      int n_src, int* status) {
   pdl_trigger();
   pdl_wait();
   __shared__ float red[8];
   const int i = blockIdx.x;
   const int src = rows ? rows[i] : i;
+  if (src < 0 || src >= n_src) {
+    if (threadIdx.x == 0) set_status(status, kStatusBadIndex);
+    for (int j = threadIdx.x; j < dim; j += 256) y[(size_t)i * dim + j] = from_f<T>(0.f);
+    return;
+  }
   const T* xr = x + (size_t)src * dim;
   T* yr = y + (size_t)i * dim;
   constexpr int EPV = 16 / sizeof(T);              // elements per 16-byte vector
@@ -161,6 +168,14 @@ __global__ void __launch_bounds__(256) rope_kv_kernel(T* __restrict__ qkv, const
 // so a query's result does not depend on the other queries of the launch (a fully masked
 // tile leaves the running max, sum and output unchanged).
 
+// A work item's block must lie inside the launch's tokens and its key range inside its cache row
+// (the exported attention entry point takes caller-built metadata); an invalid item sets
+// kStatusBadIndex and its CTA returns before touching memory.
+__device__ __forceinline__ bool attn_item_ok(const AttnGeom& g, int b, int t0, int start, int T, int row, int pos0) {
+  return b >= 0 && b < g.n_blocks && T > 0 && t0 >= 0 && t0 < T && start >= 0 && start + T <= g.n_tokens &&
+         row >= 0 && row < g.max_batch && pos0 >= 0 && pos0 + T <= g.max_seq;
+}
+
 // fp32 (parity path): scalar online softmax, one warp per query row.
 template <int D>
 __global__ void __launch_bounds__(128) attn_f32_kernel(AttnGeom g, int item_tokens, const float* __restrict__ q,
@@ -176,7 +191,15 @@ __global__ void __launch_bounds__(128) attn_f32_kernel(AttnGeom g, int item_toke
   float* Vs = Ks + KT * DP;         // [KT][D]
   const int item = blockIdx.x, kvh = blockIdx.y;
   const int b = items[2 * item], t0 = items[2 * item + 1];
+  if (b < 0 || b >= g.n_blocks) {
+    if (threadIdx.x == 0) set_status(g.status, kStatusBadIndex);
+    return;
+  }
   const int start = blk[4 * b], T = blk[4 * b + 1], row = blk[4 * b + 2], pos0 = blk[4 * b + 3];
+  if (!attn_item_ok(g, b, t0, start, T, row, pos0)) {
+    if (threadIdx.x == 0) set_status(g.status, kStatusBadIndex);
+    return;
+  }
   const int G = g.n_heads / g.n_kv_heads;
   const int nt = min(item_tokens, T - t0);
   const int nrows = nt * G;
@@ -310,7 +333,15 @@ __global__ void __launch_bounds__(WARPS * 32, MINB) attn_bf16_kernel(const __gri
 
   const int item = blockIdx.x, kvh = blockIdx.y;
   const int b = items[2 * item], t0 = items[2 * item + 1];
+  if (b < 0 || b >= g.n_blocks) {
+    if (threadIdx.x == 0) set_status(status, kStatusBadIndex);
+    return;
+  }
   const int start = blk[4 * b], T = blk[4 * b + 1], row = blk[4 * b + 2], pos0 = blk[4 * b + 3];
+  if (!attn_item_ok(g, b, t0, start, T, row, pos0)) {
+    if (threadIdx.x == 0) set_status(status, kStatusBadIndex);
+    return;
+  }
   const int G = g.n_heads / g.n_kv_heads;
   const int nt = min(item_tokens, T - t0);
   const int nrows = min(nt * G, RMAX);                  // the launcher picks RMAX >= nt * G
@@ -336,7 +367,9 @@ __global__ void __launch_bounds__(WARPS * 32, MINB) attn_bf16_kernel(const __gri
   // With the in-kernel append, tiles below the first appended key are loaded while the append
   // runs; the rest wait for it.
   const int n_pre = app.on ? min(min(NS - 1, n_tiles), (pos0 + t0) / KT) : min(NS - 1, n_tiles);
+  int n_issued = 0;                     // thread 0: key tiles issued so far (in tile order)
   auto issue = [&](int tile) {
+    n_issued = tile + 1;
     const int s = tile % NS;
     const uint32_t fb = smem_u32(&full[s]);
     const uint32_t dst = smem_u32(stages + s * STAGE);
@@ -464,7 +497,7 @@ __global__ void __launch_bounds__(WARPS * 32, MINB) attn_bf16_kernel(const __gri
 
   for (int tile = 0; tile < n_tiles; ++tile) {
     if (threadIdx.x == 0 && tile + NS - 1 < n_tiles) issue(tile + NS - 1);
-    if (!mbar_wait(smem_u32(&full[tile % NS]), (tile / NS) & 1, abort_flag)) {
+    if (!mbar_wait(smem_u32(&full[tile % NS]), (tile / NS) & 1, abort_flag, g.spin)) {
       set_status(status, kStatusTimeoutMma);
       *abort_flag = 1;
     }
@@ -552,6 +585,19 @@ __global__ void __launch_bounds__(WARPS * 32, MINB) attn_bf16_kernel(const __gri
       }
     }
     __syncthreads();
+    if (*abort_flag) break;   // set before this barrier only, so every thread leaves together
+  }
+  if (*abort_flag) {
+    // A wait gave up: no tile is issued after it, and every stage holds at most one outstanding
+    // load (a stage is refilled only after its previous tile was waited for), so waiting for the
+    // last tile issued into each stage lets every copy land before the CTA exits.
+    if (threadIdx.x == 0)
+      for (int st = 0; st < NS && st < n_issued; ++st) {
+        const int last = st + (n_issued - 1 - st) / NS * NS;
+        mbar_drain(smem_u32(&full[st]), (uint32_t)(last / NS) & 1u);
+      }
+    __syncthreads();
+    return;
   }
   // ---- merge the four key quarters' partial states in quarter order (stage memory is free now)
   constexpr int OLD = D + 4;
@@ -726,11 +772,16 @@ __global__ void round_advance_kernel(const int32_t* __restrict__ act, int n, con
   if (slot >= 0 && slot < max_batch) pos[slot] += acc[i] + 1;
 }
 
-__global__ void keys_to_ids_kernel(const unsigned long long* __restrict__ keys, int32_t* __restrict__ ids, int n) {
+// argmax keys -> token ids.  With a status word: a non-zero word (a timed-out wait or a bad row in
+// the kernels before) turns every id into -1, and the word is copied to status_out (nullable).
+__global__ void keys_to_ids_kernel(const unsigned long long* __restrict__ keys, int32_t* __restrict__ ids, int n,
+                                   const int* status, int32_t* status_out) {
   pdl_trigger();
   pdl_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < n) ids[i] = (int32_t)(0xFFFFFFFFu - (uint32_t)(keys[i] & 0xFFFFFFFFull));
+  const int st = status ? *(volatile const int*)status : 0;
+  if (i == 0 && status_out) *status_out = st;
+  if (i < n) ids[i] = st ? -1 : (int32_t)(0xFFFFFFFFu - (uint32_t)(keys[i] & 0xFFFFFFFFull));
 }
 
 // argmax over logits rows (lowest index on ties, as torch.argmax)
@@ -829,12 +880,14 @@ int attn_item_tokens(int n_heads, int n_kv_heads) {
 }
 
 int launch_rmsnorm(int dtype, const void* x, const int32_t* rows, const void* w, void* y, int n, int dim, float eps,
-                   cudaStream_t s) {
+                   cudaStream_t s, int n_src, int* status) {
   if (n <= 0) return EESD_OK;
   if (dtype == EESD_BF16)
-    launch_pdl(rmsnorm_kernel<bf16>, dim3(n), dim3(256), 0, s, (const bf16*)x, rows, (const bf16*)w, (bf16*)y, dim, eps);
+    launch_pdl(rmsnorm_kernel<bf16>, dim3(n), dim3(256), 0, s, (const bf16*)x, rows, (const bf16*)w, (bf16*)y, dim, eps,
+               n_src, status);
   else
-    launch_pdl(rmsnorm_kernel<float>, dim3(n), dim3(256), 0, s, (const float*)x, rows, (const float*)w, (float*)y, dim, eps);
+    launch_pdl(rmsnorm_kernel<float>, dim3(n), dim3(256), 0, s, (const float*)x, rows, (const float*)w, (float*)y, dim,
+               eps, n_src, status);
   return launched();
 }
 
@@ -869,14 +922,17 @@ int launch_attn_variant(dim3 grid, cudaStream_t s, const CUtensorMap& kmap, cons
   return EESD_OK;
 }
 
-int launch_attention(int dtype, const AttnGeom& g, const void* q, const void* kc, const void* vc, void* out,
+int launch_attention(int dtype, const AttnGeom& g_in, const void* q, const void* kc, const void* vc, void* out,
                      const int32_t* blk, const int32_t* items, int n_items, int max_ctx, int* status, cudaStream_t s,
                      const CUtensorMap* kmap, const CUtensorMap* vmap, int layer, const AttnAppend& app,
                      int rows_max) {
   (void)max_ctx;
   if (app.on && (dtype != EESD_BF16 || !app.kc || !app.vc || !app.cos || !app.sin)) return EESD_ERR_ARG;
   if (n_items <= 0) return EESD_OK;
-  const int it = attn_item_tokens(g.n_heads, g.n_kv_heads);
+  const int it = attn_item_tokens(g_in.n_heads, g_in.n_kv_heads);
+  AttnGeom g = g_in;
+  g.status = status;
+  g.spin = spin_limit();
   dim3 grid(n_items, g.n_kv_heads);
   if (dtype == EESD_BF16) {
     if (!kmap || !vmap) return EESD_ERR_ARG;
@@ -961,9 +1017,10 @@ int launch_round_advance(const int32_t* act, int n, const int32_t* acc, int32_t*
   launch_pdl(round_advance_kernel, dim3((n + 127) / 128), dim3(128), 0, s, act, n, acc, pos, max_batch);
   return launched();
 }
-int launch_keys_to_ids(const unsigned long long* keys, int32_t* ids, int n, cudaStream_t s) {
+int launch_keys_to_ids(const unsigned long long* keys, int32_t* ids, int n, cudaStream_t s, const int* status,
+                       int32_t* status_out) {
   if (n <= 0) return EESD_OK;
-  launch_pdl(keys_to_ids_kernel, dim3((n + 255) / 256), dim3(256), 0, s, keys, ids, n);
+  launch_pdl(keys_to_ids_kernel, dim3((n + 255) / 256), dim3(256), 0, s, keys, ids, n, status, status_out);
   return launched();
 }
 int launch_argmax_rows(int dtype, const void* logits, int n, int vocab, int32_t* ids, cudaStream_t s) {

@@ -12,14 +12,19 @@ struct AttnGeom {
   int max_batch, max_seq;
   int ld_q;          // elements between consecutive tokens' q rows (the fused qkv row)
   float scale;       // 1 / sqrt(head_dim)
+  int n_tokens, n_blocks;   // of the packed batch: items and blocks are checked against them
+  uint32_t spin;     // poll limit of the key-tile waits (spin_limit())
+  int* status;       // device status word (fp32 kernel; the bf16 kernel takes it as an argument)
 };
 
 int attn_item_tokens(int n_heads, int n_kv_heads);
 // record the text eesd_last_error() returns for the calling thread
 void set_last_error(const char* msg);
 
+// rows (nullable): source row of each output row, checked against [0, n_src) (a bad one sets
+// kStatusBadIndex in *status and zeroes its output row)
 int launch_rmsnorm(int dtype, const void* x, const int32_t* rows, const void* w, void* y, int n, int dim, float eps,
-                   cudaStream_t s);
+                   cudaStream_t s, int n_src = 0x7fffffff, int* status = nullptr);
 int launch_rope_kv(int dtype, void* qkv, const int32_t* tok_pos, const int32_t* tok_row, int n_tok, int n_heads,
                    int n_kv_heads, int head_dim, const float* cos, const float* sin, void* kc, void* vc, int max_batch,
                    int max_seq, int* status, cudaStream_t s);
@@ -51,7 +56,9 @@ int launch_greedy_accept(const int32_t* y, const int32_t* vinfo, int nv, int32_t
 int launch_round_meta(const int32_t* act, int n, const int32_t* pos, int max_batch, int cols, int item_tokens,
                       int32_t* out, cudaStream_t s);
 int launch_round_advance(const int32_t* act, int n, const int32_t* acc, int32_t* pos, int max_batch, cudaStream_t s);
-int launch_keys_to_ids(const unsigned long long* keys, int32_t* ids, int n, cudaStream_t s);
+// status (nullable): a non-zero word makes every id -1; status_out (nullable) receives the word
+int launch_keys_to_ids(const unsigned long long* keys, int32_t* ids, int n, cudaStream_t s,
+                       const int* status = nullptr, int32_t* status_out = nullptr);
 int launch_argmax_rows(int dtype, const void* logits, int n, int vocab, int32_t* ids, cudaStream_t s);
 int launch_swiglu_f32(const float* gu, float* out, int n, int inter, cudaStream_t s);
 int launch_simt_gemm_f32(int epi, const float* x, const float* w, const float* residual, float* y, int n_tok, int n_out,

@@ -20,6 +20,7 @@ namespace eesd {
 namespace {
 
 thread_local std::string g_err;
+uint32_t g_spin_limit = kSpinLimit;   // pipeline-wait poll limit (EESD_OPT_SPIN_LIMIT)
 
 int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
 int fail(int code, const char* fmt, ...) {
@@ -166,6 +167,7 @@ int check_batch(const Model* m, const EesdBatch* b) {
 }  // namespace
 
 void set_last_error(const char* msg) { g_err = msg; }
+uint32_t spin_limit() { return g_spin_limit; }
 
 }  // namespace eesd
 
@@ -288,7 +290,7 @@ int eesd_forward_layers(void* h, void* x, const EesdBatch* b, int start, int end
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const size_t layer_kv = (size_t)d.max_batch * d.n_kv_heads * d.max_seq * d.head_dim * m->eb;
   AttnGeom g{d.n_heads, d.n_kv_heads, d.head_dim, d.max_batch, d.max_seq, m->qkv_dim,
-             1.0f / sqrtf((float)d.head_dim)};
+             1.0f / sqrtf((float)d.head_dim), N, b->n_blocks, 0u, nullptr};
   ProfEvent pe;
   // query rows of the largest attention work item: one token per block (draft) or up to a full item
   const int G = d.n_heads / d.n_kv_heads;
@@ -583,6 +585,62 @@ int eesd_status_read(const int32_t* status, int* bits_out, void* stream) {
   return bits ? fail(EESD_ERR_DEVICE, "device status bits 0x%x", bits) : EESD_OK;
 }
 
+int eesd_attn_varlen_gqa(int dtype, const void* qkv, int n_heads, int n_kv_heads, int head_dim, void* k_cache,
+                         void* v_cache, int max_batch, int max_seq, const EesdBatch* b, int append,
+                         const float* rope_cos, const float* rope_sin, void* out, int32_t* status, void* stream) {
+  if (!qkv || !k_cache || !v_cache || !out || !b) return fail(EESD_ERR_ARG, "attn: null argument");
+  if (dtype != EESD_BF16 && dtype != EESD_F32) return fail(EESD_ERR_ARG, "attn: dtype %d", dtype);
+  if (n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads || (head_dim != 64 && head_dim != 128))
+    return fail(EESD_ERR_ARG, "attn: heads %d / %d, head_dim %d (64 or 128)", n_heads, n_kv_heads, head_dim);
+  if (max_batch <= 0 || max_seq <= 0 || max_seq % 64) return fail(EESD_ERR_ARG, "attn: max_seq must be a multiple of 64");
+  if (b->n_tokens < 0 || b->n_blocks < 0 || b->n_items < 0) return fail(EESD_ERR_ARG, "attn: negative batch sizes");
+  if (b->n_tokens == 0 || b->n_items == 0) return EESD_OK;
+  if (!b->blk || !b->items || b->n_blocks <= 0) return fail(EESD_ERR_ARG, "attn: missing block metadata");
+  if (b->max_ctx > max_seq) return fail(EESD_ERR_ARG, "attn: max_ctx %d > max_seq %d", b->max_ctx, max_seq);
+  const long long cache_rows = (long long)max_batch * n_kv_heads * max_seq;
+  if (cache_rows >= (1LL << 31)) return fail(EESD_ERR_ARG, "attn: cache too large for 32-bit TMA row coordinates");
+  AttnAppend app;
+  if (append) {
+    if (dtype != EESD_BF16) return fail(EESD_ERR_ARG, "attn: the in-kernel RoPE/append path is bf16 only");
+    if (b->n_items != b->n_blocks)
+      return fail(EESD_ERR_ARG, "attn: append needs every block to be one work item (n_items == n_blocks)");
+    if (!rope_cos || !rope_sin) return fail(EESD_ERR_ARG, "attn: append needs the RoPE tables");
+    app.on = true;
+    app.kc = k_cache;
+    app.vc = v_cache;
+    app.cos = rope_cos;
+    app.sin = rope_sin;
+  }
+  const int qkv_dim = (n_heads + 2 * n_kv_heads) * head_dim;
+  AttnGeom g{n_heads, n_kv_heads, head_dim, max_batch, max_seq, qkv_dim, 1.0f / sqrtf((float)head_dim), b->n_tokens,
+             b->n_blocks, 0u, nullptr};
+  CUtensorMap kmap, vmap;
+  if (dtype == EESD_BF16) {
+    if (encode_kmajor_map(&kmap, k_cache, (int)cache_rows, head_dim, 64) ||
+        encode_kmajor_map(&vmap, v_cache, (int)cache_rows, head_dim, 64))
+      return fail(EESD_ERR_ARG, "attn: KV cache tensor map (16-byte aligned bf16 caches required)");
+  }
+  const int G = n_heads / n_kv_heads;
+  const int rows_max = b->n_tokens == b->n_blocks ? G : attn_item_tokens(n_heads, n_kv_heads) * G;
+  const int rc = launch_attention(dtype, g, qkv, k_cache, v_cache, out, b->blk, b->items, b->n_items, b->max_ctx,
+                                  status, static_cast<cudaStream_t>(stream), &kmap, &vmap, 0, app, rows_max);
+  return rc ? fail(rc, "attention launch") : EESD_OK;
+}
+
+int eesd_rope_kv_append(int dtype, void* qkv, const int32_t* tok_pos, const int32_t* tok_row, int n_tok, int n_heads,
+                        int n_kv_heads, int head_dim, const float* rope_cos, const float* rope_sin, void* k_cache,
+                        void* v_cache, int max_batch, int max_seq, int32_t* status, void* stream) {
+  if (!qkv || !tok_pos || !tok_row || !rope_cos || !rope_sin || !k_cache || !v_cache || n_tok < 0)
+    return fail(EESD_ERR_ARG, "rope_kv_append: null argument or n_tok < 0");
+  if (dtype != EESD_BF16 && dtype != EESD_F32) return fail(EESD_ERR_ARG, "rope_kv_append: dtype %d", dtype);
+  if (n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads || (head_dim != 64 && head_dim != 128))
+    return fail(EESD_ERR_ARG, "rope_kv_append: heads %d / %d, head_dim %d", n_heads, n_kv_heads, head_dim);
+  if (max_batch <= 0 || max_seq <= 0) return fail(EESD_ERR_ARG, "rope_kv_append: cache sizes");
+  const int rc = launch_rope_kv(dtype, qkv, tok_pos, tok_row, n_tok, n_heads, n_kv_heads, head_dim, rope_cos, rope_sin,
+                                k_cache, v_cache, max_batch, max_seq, status, static_cast<cudaStream_t>(stream));
+  return rc ? fail(rc, "rope_kv_append launch") : EESD_OK;
+}
+
 int eesd_set_option(int option, int value) {
   if (option == 1) {   // tcgen05 MMA N: 0 = whole token tile, else a fixed multiple of 16
     if (value < 0 || value > 256 || value % 16) return fail(EESD_ERR_ARG, "mma n %d", value);
@@ -607,6 +665,11 @@ int eesd_set_option(int option, int value) {
   if (option == 5) {   // LM head: two row tiles per CTA up to 256 tokens: 1 = on (default), 0 = off
     if (value < 0 || value > 1) return fail(EESD_ERR_ARG, "head two tiles %d", value);
     tc_set_head_two_tiles(value);
+    return EESD_OK;
+  }
+  if (option == 6) {   // pipeline-wait poll limit: -1 = the default, n >= 0 = n polls (0: every wait gives up)
+    if (value < -1) return fail(EESD_ERR_ARG, "spin limit %d", value);
+    g_spin_limit = value < 0 ? kSpinLimit : (uint32_t)value;
     return EESD_OK;
   }
   return fail(EESD_ERR_ARG, "unknown option %d", option);

@@ -13,7 +13,7 @@ LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libeesd.so"
 OK, ERR_ARG, ERR_CUDA, ERR_DEVICE = 0, 1, 2, 3
 BF16, F32 = 0, 1
 EPI_STORE, EPI_RESIDUAL, EPI_SWIGLU = 0, 1, 2
-OPT_MMA_N, OPT_SPLITS, OPT_STAGES, OPT_PAIR, OPT_HEAD_TWO_TILES = 1, 2, 3, 4, 5
+OPT_MMA_N, OPT_SPLITS, OPT_STAGES, OPT_PAIR, OPT_HEAD_TWO_TILES, OPT_SPIN_LIMIT = 1, 2, 3, 4, 5, 6
 PROF_KINDS = 9
 PROF_NAMES = ["norm", "gemm_qkv", "rope_kv", "attn", "gemm_o", "gemm_w13", "gemm_w2", "head", "misc"]
 
@@ -67,7 +67,11 @@ SIGNATURES = {
     "eesd_gemm": (C.c_int, [C.c_int, C.c_int, vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, vp, sz, vp]),
     "eesd_set_option": (C.c_int, [C.c_int, C.c_int]),
     "eesd_status_read": (C.c_int, [vp, C.POINTER(C.c_int), vp]),
-    "eesd_head_argmax_static": (C.c_int, [vp, vp, C.c_int, C.c_int, C.c_int, vp, vp, C.c_float, vp, vp]),
+    "eesd_head_argmax_static": (C.c_int, [vp, C.c_int, vp, C.c_int, C.c_int, C.c_int, vp, vp, C.c_float, vp, vp, vp]),
+    "eesd_attn_varlen_gqa": (C.c_int, [C.c_int, vp, C.c_int, C.c_int, C.c_int, vp, vp, C.c_int, C.c_int,
+                                       C.POINTER(Batch), C.c_int, vp, vp, vp, vp, vp]),
+    "eesd_rope_kv_append": (C.c_int, [C.c_int, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, vp, vp, vp, vp,
+                                      C.c_int, C.c_int, vp, vp]),
 }
 
 _lib = None
@@ -101,7 +105,7 @@ def check(rc: int, what: str = "") -> None:
 # entry points that launch exactly one kernel (counted for the bench's launch total)
 KERNEL_CALLS = {"eesd_pack_weight", "eesd_copy_rows", "eesd_gather_ids", "eesd_scatter_ids", "eesd_greedy_accept",
                 "eesd_round_meta", "eesd_round_advance", "eesd_rmsnorm",
-                "eesd_gemm"}
+                "eesd_gemm", "eesd_attn_varlen_gqa", "eesd_rope_kv_append"}
 direct_launches = 0
 
 
