@@ -334,8 +334,9 @@ def run_ours(args) -> None:
     import torch.distributed as dist
 
     from thesis_b200.config import preset
-    from thesis_b200.eesd import B200SpecEngine
+    from thesis_b200.eesd import B200ARBatchEngine, B200SpecEngine
     from thesis_b200.engine import RunConfig
+    from thesis_b200.shard import gather_outputs, shard_requests
     from thesis_b200.model import ModelWeights
     from thesis_b200.synthetic import synthetic_prompts
     from thesis_b200 import lib
@@ -354,8 +355,6 @@ def run_ours(args) -> None:
                                residual_scale=0.1)
     if args.strong:
         # strong scaling: the 64 requests of the 1-GPU run, sharded over the ranks
-        from thesis_b200.shard import shard_requests
-
         allp = synthetic_prompts(B_PER_GPU, cfg.vocab_size, seed=1000, min_len=PROMPT_LEN[0], max_len=PROMPT_LEN[1])
         ids = shard_requests(B_PER_GPU, rank, world)
         prompts = [allp[i] for i in ids]
@@ -377,8 +376,6 @@ def run_ours(args) -> None:
     if world > 1:
         # the output gather's first NCCL all_gather sets up its channels (~30 ms, once per process);
         # it is warmed here like the steps, and runs again inside the timed region
-        from thesis_b200.shard import gather_outputs
-
         gather_outputs({ids[i]: eng.slots[i].output for i in range(nb)}, n_total, world, device=dev)
     stream = torch.cuda.current_stream()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -462,12 +459,72 @@ def run_ours(args) -> None:
                 "frac": (1000 * nbytes / hbm) / ms if ms else None}
     share = {f"{k}@{n}": round(v[1] / total_ms, 4) for (k, n), v in sorted(groups.items(), key=lambda kv: -kv[1][1])}
 
+    # ---- losslessness on the headline workload: the speculative output of a fixed subset of the
+    # requests equals the same engine's autoregressive output, token for token
+    lossless = None
+    if args.lossless_requests > 0:
+        sub = prompts[:args.lossless_requests]
+        rc_ll = RunConfig(mode="static", keep_outputs=True)
+        toks = []
+        for make in (lambda: B200ARBatchEngine(w, len(sub), PROMPT_LEN[1], args.lossless_new, (), ignore_eos=True),
+                     lambda: B200SpecEngine(w, len(sub), PROMPT_LEN[1], args.lossless_new, (), ignore_eos=True,
+                                            exit_layer=EXIT, gamma=GAMMA)):
+            e = make()
+            res = e.run(sub, rc_ll)
+            by = {c["pid"]: c["tokens"] for c in res["completions"]}
+            toks.append([by[p.pid] for p in sub])
+            e.free()
+        lossless = {"spec_equals_ar": toks[0] == toks[1], "requests": len(sub), "new_tokens": args.lossless_new,
+                    "check": "B200SpecEngine vs B200ARBatchEngine token lists on the first requests of this rank"}
+    eng.free()
+    del eng
+    torch.cuda.empty_cache()
+
+    # ---- strong scaling next to weak scaling (multi-GPU runs): the 64 requests of the 1-GPU run
+    # sharded over the ranks, run concurrently, timed like the weak case
+    strong = None
+    if world > 1 and not args.strong and not args.no_strong_sub:
+        allp = synthetic_prompts(B_PER_GPU, cfg.vocab_size, seed=1000, min_len=PROMPT_LEN[0], max_len=PROMPT_LEN[1])
+        sids = shard_requests(B_PER_GPU, rank, world)
+        sp_prompts = [allp[i] for i in sids]
+        s_eng = B200SpecEngine(w, len(sp_prompts), PROMPT_LEN[1], MAX_NEW, (), ignore_eos=True, exit_layer=EXIT,
+                               gamma=GAMMA)
+        s_eng.start(sp_prompts)
+        for _ in range(args.warmup):
+            s_eng.step(measured=False)
+        gather_outputs({sids[i]: s_eng.slots[i].output for i in range(len(sids))}, B_PER_GPU, world, device=dev)
+        n0 = len(s_eng.records)
+        dist.barrier()
+        torch.cuda.synchronize()
+        s_committed = 0
+        ev0.record(stream)
+        for _ in range(args.steps):
+            s_committed += s_eng.step(measured=True)
+        gather_outputs({sids[i]: s_eng.slots[i].output for i in range(len(sids))}, B_PER_GPU, world, device=dev)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        dist.barrier()
+        st = torch.tensor([ev0.elapsed_time(ev1), float(s_committed)], dtype=torch.float64, device=dev)
+        per = [torch.zeros_like(st) for _ in range(world)]
+        dist.all_gather(per, st)
+        s_ms = max(float(x[0]) for x in per)
+        s_tok = sum(float(x[1]) for x in per)
+        sv = [r.forward_ms for r in s_eng.records[n0:] if r.kind == "verify"]
+        sd = [r.forward_ms for r in s_eng.records[n0:] if r.kind == "draft"]
+        strong = {"value": s_tok / (s_ms / 1000.0), "unit": "tokens/s", "requests_total": B_PER_GPU,
+                  "requests_per_gpu": len(sids), "ms_per_step": s_ms / args.steps,
+                  "rank_ms_per_step": [round(float(x[0]) / args.steps, 3) for x in per],
+                  "verify_step_p50_ms": statistics.median(sv) if sv else None,
+                  "draft_step_p50_ms": statistics.median(sd) if sd else None,
+                  "limiter": (f"every rank streams the full 16 GB of weights per round for {len(sids)} requests "
+                              "(weight-bound steps), plus the final NCCL all_gather of the outputs")}
+        s_eng.free()
+        del s_eng
+        torch.cuda.empty_cache()
+
     # ---- end to end through the public engine API (host prompts in, token lists out)
     e2e = None
     if not args.no_e2e:
-        eng.free()
-        del eng
-        torch.cuda.empty_cache()
         e2e_eng = B200SpecEngine(w, nb, PROMPT_LEN[1], args.e2e_new, (), ignore_eos=True, exit_layer=EXIT,
                                  gamma=GAMMA)
         if world > 1:
@@ -532,6 +589,8 @@ def run_ours(args) -> None:
                              "context; activations excluded"},
             "e2e": e2e,
             "cpu_baseline": cb,
+            "lossless": lossless,
+            "strong": strong,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -551,6 +610,11 @@ def main():
     ap.add_argument("--strong", action="store_true",
                     help="strong scaling: the 64 requests of the 1-GPU run sharded over the GPUs (default: 64 per GPU)")
     ap.add_argument("--profile-rounds", type=int, default=3, help="profiled rounds after the timed region")
+    ap.add_argument("--lossless-requests", type=int, default=8,
+                    help="requests of the speculative == autoregressive check after the timed region (0 = skip)")
+    ap.add_argument("--lossless-new", type=int, default=64, help="new tokens per request of that check")
+    ap.add_argument("--no-strong-sub", action="store_true",
+                    help="multi-GPU runs: skip the strong-scaling measurement reported next to weak scaling")
     ap.add_argument("--tokens-per-round", type=float, default=TOKENS_PER_ROUND,
                     help="reference arm: tokens committed per round (default: the B200 engine's measured value "
                          "on this workload)")
