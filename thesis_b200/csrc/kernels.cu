@@ -386,95 +386,90 @@ __global__ void __launch_bounds__(WARPS * 32, MINB) attn_bf16_kernel(const __gri
     for (int t = 0; t < n_pre; ++t) issue(t);
   }
   if (app.on) {
-    // RoPE (rotate-half, reference bf16 roundings as in the rope/KV kernel) for this item's tokens:
-    // k rotated and v copied into the cache first, then the proxy fence orders those generic
-    // stores before the TMA reads of the same key tiles; q is rotated in shared memory.
+    // RoPE (rotate-half, reference bf16 roundings as in the rope/KV kernel) and the KV append for
+    // this item's tokens, in one pass: every global load (k, v, cos, sin) is issued while the Q rows
+    // land by cp.async; after one barrier each thread rotates its (token, pair) of k and writes it to
+    // the cache, writes its v chunk, and rotates the same pair of the token's G query rows in shared
+    // memory with the same cos / sin.  The proxy fence orders the cache stores before the TMA reads of
+    // those key tiles, which are issued only after the second barrier.
     const int half = D / 2;
     const bool valid = row >= 0 && row < g.max_batch && pos0 >= 0 && pos0 + t0 + nt <= g.max_seq;
-    if (!valid) {
-      if (threadIdx.x == 0) set_status(status, kStatusBadIndex);
-    } else {
-      bf16* kc = static_cast<bf16*>(app.kc) + ((size_t)row * g.n_kv_heads + kvh) * g.max_seq * D;
-      bf16* vc = static_cast<bf16*>(app.vc) + ((size_t)row * g.n_kv_heads + kvh) * g.max_seq * D;
-      constexpr int kU = 4;   // independent (token, pair) items per thread in flight
-      for (int i0 = threadIdx.x; i0 < nt * half; i0 += kU * NT) {
-        float x1[kU], x2[kU], c1[kU], c2[kU], s1[kU], s2[kU];
+    if (!valid && threadIdx.x == 0) set_status(status, kStatusBadIndex);
+    bf16* kc = static_cast<bf16*>(app.kc) + ((size_t)row * g.n_kv_heads + kvh) * g.max_seq * D;
+    bf16* vc = static_cast<bf16*>(app.vc) + ((size_t)row * g.n_kv_heads + kvh) * g.max_seq * D;
+    constexpr int kU = 4;     // (token, pair) items per thread and pass
+    constexpr int kV = 2;     // 16-byte v chunks per thread and pass
+    const int n_k = valid ? nt * half : 0, n_v = valid ? nt * (D / 8) : 0;
+    const int passes = max((n_k + kU * NT - 1) / (kU * NT), (n_v + kV * NT - 1) / (kV * NT));   // same on every thread
+    for (int ps = 0; ps < passes; ++ps) {
+      float x1[kU], x2[kU], c1[kU], c2[kU], s1[kU], s2[kU];
+      uint4 vv[kV];
 #pragma unroll
-        for (int u = 0; u < kU; ++u) {
-          const int i = i0 + u * NT;
-          if (i < nt * half) {
-            const int tt = i / half, d = i - tt * half, pos = pos0 + t0 + tt;
-            const bf16* src = q + (size_t)(start + t0 + tt) * g.ld_q + (g.n_heads + kvh) * D;
-            x1[u] = __bfloat162float(__ldg(src + d));
-            x2[u] = __bfloat162float(__ldg(src + d + half));
-            c1[u] = __ldg(app.cos + (size_t)pos * D + d);
-            c2[u] = __ldg(app.cos + (size_t)pos * D + d + half);
-            s1[u] = __ldg(app.sin + (size_t)pos * D + d);
-            s2[u] = __ldg(app.sin + (size_t)pos * D + d + half);
-          }
-        }
-#pragma unroll
-        for (int u = 0; u < kU; ++u) {
-          const int i = i0 + u * NT;
-          if (i < nt * half) {
-            const int tt = i / half, d = i - tt * half, pos = pos0 + t0 + tt;
-            const float k1 = rnd<bf16>(x1[u] * rnd<bf16>(c1[u])) + rnd<bf16>(-x2[u] * rnd<bf16>(s1[u]));
-            const float k2 = rnd<bf16>(x2[u] * rnd<bf16>(c2[u])) + rnd<bf16>(x1[u] * rnd<bf16>(s2[u]));
-            kc[(size_t)pos * D + d] = __float2bfloat16_rn(k1);
-            kc[(size_t)pos * D + d + half] = __float2bfloat16_rn(k2);
-          }
+      for (int u = 0; u < kU; ++u) {
+        const int i = threadIdx.x + (ps * kU + u) * NT;
+        if (i < n_k) {
+          const int tt = i / half, d = i - tt * half, pos = pos0 + t0 + tt;
+          const bf16* src = q + (size_t)(start + t0 + tt) * g.ld_q + (g.n_heads + kvh) * D;
+          x1[u] = __bfloat162float(__ldg(src + d));
+          x2[u] = __bfloat162float(__ldg(src + d + half));
+          c1[u] = __ldg(app.cos + (size_t)pos * D + d);
+          c2[u] = __ldg(app.cos + (size_t)pos * D + d + half);
+          s1[u] = __ldg(app.sin + (size_t)pos * D + d);
+          s2[u] = __ldg(app.sin + (size_t)pos * D + d + half);
         }
       }
-      for (int i = threadIdx.x; i < nt * (D / 8); i += NT) {
-        const int tt = i / (D / 8), c8 = i - tt * (D / 8), pos = pos0 + t0 + tt;
-        const uint4* src = reinterpret_cast<const uint4*>(q + (size_t)(start + t0 + tt) * g.ld_q +
-                                                          (g.n_heads + g.n_kv_heads + kvh) * D) + c8;
-        reinterpret_cast<uint4*>(vc + (size_t)pos * D)[c8] = *src;
-      }
-      asm volatile("fence.proxy.async.global;" ::: "memory");
-    }
-    cp_async_wait<0>();
-    __syncthreads();
-    if (valid) {
-      // thread -> rotation pair d of one token group; the G rows of a token share cos / sin
-      const int groups = NT / half;
-      const int d = threadIdx.x % half;
-      constexpr int kU = 4;
-      for (int tt0 = threadIdx.x / half; tt0 < nt; tt0 += kU * groups) {
-        float c1[kU], c2[kU], s1[kU], s2[kU];
 #pragma unroll
-        for (int u = 0; u < kU; ++u) {
-          const int tt = tt0 + u * groups;
-          if (tt < nt) {
-            const int pos = pos0 + t0 + tt;
-            c1[u] = __ldg(app.cos + (size_t)pos * D + d);
-            c2[u] = __ldg(app.cos + (size_t)pos * D + d + half);
-            s1[u] = __ldg(app.sin + (size_t)pos * D + d);
-            s2[u] = __ldg(app.sin + (size_t)pos * D + d + half);
-          }
+      for (int u = 0; u < kV; ++u) {
+        const int i = threadIdx.x + (ps * kV + u) * NT;
+        if (i < n_v) {
+          const int tt = i / (D / 8), c8 = i - tt * (D / 8);
+          vv[u] = __ldg(reinterpret_cast<const uint4*>(q + (size_t)(start + t0 + tt) * g.ld_q +
+                                                       (g.n_heads + g.n_kv_heads + kvh) * D) + c8);
         }
+      }
+      if (ps == 0) {            // the Q rows (every thread's cp.async) are in shared memory after this
+        cp_async_wait<0>();
+        __syncthreads();
+      }
 #pragma unroll
-        for (int u = 0; u < kU; ++u) {
-          const int tt = tt0 + u * groups;
-          if (tt < nt) {
-            const float cc1 = rnd<bf16>(c1[u]), cc2 = rnd<bf16>(c2[u]), ss1 = rnd<bf16>(s1[u]), ss2 = rnd<bf16>(s2[u]);
-            for (int gh = 0; gh < G; ++gh) {
-              bf16* qr = Qs + (tt * G + gh) * LDQ;
-              const float x1 = __bfloat162float(qr[d]), x2 = __bfloat162float(qr[d + half]);
-              qr[d] = __float2bfloat16_rn(rnd<bf16>(x1 * cc1) + rnd<bf16>(-x2 * ss1));
-              qr[d + half] = __float2bfloat16_rn(rnd<bf16>(x2 * cc2) + rnd<bf16>(x1 * ss2));
-            }
+      for (int u = 0; u < kV; ++u) {
+        const int i = threadIdx.x + (ps * kV + u) * NT;
+        if (i < n_v) {
+          const int tt = i / (D / 8), c8 = i - tt * (D / 8);
+          reinterpret_cast<uint4*>(vc + (size_t)(pos0 + t0 + tt) * D)[c8] = vv[u];
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int i = threadIdx.x + (ps * kU + u) * NT;
+        if (i < n_k) {
+          const int tt = i / half, d = i - tt * half, pos = pos0 + t0 + tt;
+          const float cc1 = rnd<bf16>(c1[u]), cc2 = rnd<bf16>(c2[u]), ss1 = rnd<bf16>(s1[u]), ss2 = rnd<bf16>(s2[u]);
+          const float k1 = rnd<bf16>(x1[u] * cc1) + rnd<bf16>(-x2[u] * ss1);
+          const float k2 = rnd<bf16>(x2[u] * cc2) + rnd<bf16>(x1[u] * ss2);
+          kc[(size_t)pos * D + d] = __float2bfloat16_rn(k1);
+          kc[(size_t)pos * D + d + half] = __float2bfloat16_rn(k2);
+          for (int gh = 0; gh < G; ++gh) {          // the token's G query rows (disjoint per thread)
+            bf16* qr = Qs + (tt * G + gh) * LDQ;
+            const float y1 = __bfloat162float(qr[d]), y2 = __bfloat162float(qr[d + half]);
+            qr[d] = __float2bfloat16_rn(rnd<bf16>(y1 * cc1) + rnd<bf16>(-y2 * ss1));
+            qr[d + half] = __float2bfloat16_rn(rnd<bf16>(y2 * cc2) + rnd<bf16>(y1 * ss2));
           }
         }
       }
     }
+    if (passes == 0) {          // nothing to append (an invalid block): Q still has to land
+      cp_async_wait<0>();
+    }
+    asm volatile("fence.proxy.async.global;" ::: "memory");
     __syncthreads();
     // the tiles holding the appended keys go out only now
     if (threadIdx.x == 0)
       for (int t = n_pre; t < NS - 1 && t < n_tiles; ++t) issue(t);
+  } else {
+    cp_async_wait<0>();
+    __syncthreads();
   }
-  cp_async_wait<0>();
-  __syncthreads();
 
   const int gq = lane >> 2, tq = lane & 3;
   const int n_rg = (nrows + 15) / 16;                   // row groups with rows
