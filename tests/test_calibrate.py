@@ -11,6 +11,7 @@ from pathlib import Path
 import numpy as np
 import pytest
 
+from refpath import reference_dir
 from thesis_b200.calibrate import StepCost, fit_linear, hinge_knee, model_dims
 from thesis_b200.config import preset
 
@@ -56,10 +57,10 @@ def test_step_prices_follow_the_roofline_form():
 def test_calibration_file_loads_in_the_reference_cost_model(tmp_path):
     """The JSON layout is the one solutions/cost_model.py:load_cost_model reads, and the restated
     step prices equal the reference's own for the three model kinds.  Needs a checkout of the
-    reference (THESIS_REFERENCE)."""
-    ref = Path(os.environ.get("THESIS_REFERENCE", "/root/reference"))
-    if not (ref / "solutions" / "cost_model.py").exists():
-        pytest.skip("no checkout of the reference")
+    reference (THESIS_REFERENCE or baseline/_ref)."""
+    ref = reference_dir()
+    if ref is None:
+        pytest.skip("the reference is not available (THESIS_REFERENCE or baseline/_ref)")
     cfg = preset("llama3-8b")
     cal = _synthetic_calibration(cfg)
     path = tmp_path / "cal.json"

@@ -6,6 +6,8 @@ import argparse
 import numpy as np
 import pytest
 
+from refpath import reference_dir
+
 from thesis_b200.engine import DecodeEngine, RunConfig, StepRecord
 from thesis_b200.packing import pack, qo_indptr
 from thesis_b200.synthetic import Prompt, synthetic_prompts
@@ -145,15 +147,15 @@ def test_synthetic_inputs_are_seeded():
 def test_plugin_registers_into_the_reference_harness():
     """The drop-in boundary itself: the reference's registry takes the B200 methods through
     ``load_plugins`` and its benchmark parser accepts their flags next to the reference's own.
-    Needs a checkout of the reference (THESIS_REFERENCE); the CUDA library is not touched."""
+    Needs the reference (THESIS_REFERENCE or baseline/_ref); the CUDA library is not touched."""
     import os
     import subprocess
     import sys
     from pathlib import Path
 
-    ref = Path(os.environ.get("THESIS_REFERENCE", "/root/reference"))
-    if not (ref / "common" / "methods.py").exists():
-        pytest.skip("no checkout of the reference")
+    ref = reference_dir()
+    if ref is None:
+        pytest.skip("the reference is not available (THESIS_REFERENCE or baseline/_ref)")
     repo = Path(__file__).resolve().parents[1]
     code = f"""
 import sys

@@ -1,1 +1,3 @@
-"""B200-native packed LayerSkip-Llama draft/verify step (see DESIGN.md at the repository root)."""
+"""B200-native packed LayerSkip-Llama draft/verify step: a C-ABI library of sm_100a kernels
+(``thesis_b200/_lib/libeesd.so``, declared in ``include/eesd.h``) behind the reference's
+``DecodeEngine`` / method-registry interface."""

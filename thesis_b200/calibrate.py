@@ -45,48 +45,76 @@ N_GRID = (1, 2, 4, 8, 16, 24, 32, 48, 64, 80, 96, 112, 128, 160, 192, 224, 256, 
 
 
 def _t(fn, reps: int = 20, warm: int = 5) -> float:
-    """Median CUDA-event time of fn() in ms."""
+    """Median device time of fn() in ms: `warm` untimed calls, then `reps` calls each bracketed by
+    its own pair of CUDA events."""
     for _ in range(warm):
         fn()
     torch.cuda.synchronize()
-    ts = []
+    pairs = []
     for _ in range(reps):
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
+        ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+        ev[0].record()
         fn()
-        b.record()
-        b.synchronize()
-        ts.append(a.elapsed_time(b))
-    return float(np.median(ts))
+        ev[1].record()
+        pairs.append(ev)
+    torch.cuda.synchronize()
+    return float(np.median([a.elapsed_time(b) for a, b in pairs]))
 
 
 # ---------------------------------------------------------------------------------- fits
+def _lsq(X: np.ndarray, y: np.ndarray) -> np.ndarray:
+    """Least-squares coefficients through a QR factorisation of the design matrix."""
+    q, r = np.linalg.qr(X)
+    return np.linalg.solve(r, q.T @ y)
+
+
 def hinge_knee(ns, ms, grid=None) -> tuple:
-    """Relative-error least squares of t = a + b max(n - knee, 0) over a grid of knees (b >= 0).
+    """Knee of the hinge t(n) = a + b max(n - knee, 0), b >= 0, that minimises the squared relative
+    error.  For a fixed knee the model is linear in (a, b) and solved directly; the knee is searched
+    over the measured token counts (or `grid`), then refined inside the two neighbouring intervals
+    of the best one by golden-section search (the error is smooth between measured points).
     Returns (knee, (a, b))."""
     n = np.asarray(ns, dtype=np.float64)
     y = np.asarray(ms, dtype=np.float64)
-    wgt = 1.0 / y
-    best = None
-    for kn in (grid if grid is not None else np.arange(4.0, n.max(), 2.0)):
-        X = np.stack([np.ones_like(n), np.maximum(n - kn, 0.0)], axis=1)
-        coef = np.linalg.lstsq(X * wgt[:, None], y * wgt, rcond=None)[0]
+    w = 1.0 / y
+
+    def fit(kn: float):
+        X = np.stack([np.ones_like(n), np.maximum(n - kn, 0.0)], axis=1) * w[:, None]
+        coef = _lsq(X, y * w)
         if coef[1] < 0:
-            continue
-        err = float(np.sum(((X @ coef - y) * wgt) ** 2))
-        if best is None or err < best[0]:
-            best = (err, float(kn), (float(coef[0]), float(coef[1])))
-    if best is None:
+            return np.inf, coef
+        return float(np.sum((X @ coef - y * w) ** 2)), coef
+
+    pts = np.unique(n)
+    cand = np.asarray(grid, dtype=np.float64) if grid is not None else pts[:-1]
+    errs = [fit(k)[0] for k in cand]
+    i = int(np.argmin(errs))
+    if not np.isfinite(errs[i]):
         raise ValueError("no knee with a non-negative slope")
-    return best[1], best[2]
+    best_k, best_e = float(cand[i]), errs[i]
+    if grid is None and best_e > 0:
+        lo = pts[max(i - 1, 0)]
+        hi = pts[min(i + 1, len(pts) - 1)]
+        g = (np.sqrt(5.0) - 1) / 2
+        a, b = lo, hi
+        for _ in range(40):
+            c, d = b - g * (b - a), a + g * (b - a)
+            if fit(c)[0] < fit(d)[0]:
+                b = d
+            else:
+                a = c
+        k = 0.5 * (a + b)
+        if fit(k)[0] < best_e * (1 - 1e-9):
+            best_k, best_e = float(k), fit(k)[0]
+    coef = fit(best_k)[1]
+    return best_k, (float(coef[0]), float(coef[1]))
 
 
 def fit_linear(layer_rows, head_rows) -> dict:
-    """t_layer = a + b n + c KV (positions read), t_head = head_a + head_b n, plain least squares."""
-    X = np.array([[1.0, r["n"], r["kv"]] for r in layer_rows])
-    a, b, c = np.linalg.lstsq(X, np.array([r["ms"] for r in layer_rows]), rcond=None)[0]
-    Xh = np.array([[1.0, h["n"]] for h in head_rows])
-    ha, hb = np.linalg.lstsq(Xh, np.array([h["ms"] for h in head_rows]), rcond=None)[0]
+    """Plain least squares of t_layer = a + b n + c KV (n packed tokens, KV positions read) and
+    t_head = head_a + head_b n."""
+    a, b, c = _lsq(np.array([[1.0, r["n"], r["kv"]] for r in layer_rows]), np.array([r["ms"] for r in layer_rows]))
+    ha, hb = _lsq(np.array([[1.0, h["n"]] for h in head_rows]), np.array([h["ms"] for h in head_rows]))
     return {"a": float(a), "b": float(b), "c": float(c), "head_a": float(ha), "head_b": float(hb)}
 
 
@@ -258,8 +286,11 @@ def trace_ops(dm: DeviceModel) -> dict:
     return {"n_op_layer": float(c1 - c0), "n_op_bucket": 0.0, "n_op_head": float(c2 - c1), "n_op_segment": 1.0}
 
 
-def layer_grid(dm: DeviceModel, Bs=(1, 4, 16, 32, 64), Ts=(1, 4, 8, 17), ctxs=(256, 1024, 2048)) -> tuple:
-    """One packed layer over B requests x T tokens at context C (solutions/calibrate.py:93-113)."""
+def layer_grid(dm: DeviceModel, Bs=(1, 8, 32, 64, 128), Ts=(1, 2, 5, 9), ctxs=(128, 640, 1536)) -> tuple:
+    """One packed layer over B requests x T tokens at context C, the quantities of
+    solutions/calibrate.py:93-113.  The grid follows the engines here: draft (T = 1), verify
+    (T = gamma + 1 = 5) and per-request draft lengths up to 8 (T = 9), batches up to the
+    serving configuration's, contexts of the benchmark configurations."""
     rows, heads = [], []
     for C in ctxs:
         for B in Bs:

@@ -1,9 +1,10 @@
-"""Engine contract of the reference's benchmark harness, restated for the B200 engines.
+"""Engine contract of the reference's benchmark harness, implemented for the B200 engines.
 
-Mirrors ``common/engine.py``: ``StepRecord`` (:36-44), ``SlotState`` (:47-58), ``RunConfig``
-(:61-77), the cyclic-replay / static driver ``DecodeEngine.run`` (:178-297) and the commit rule
-``_commit`` (:144-164), with the same argument meanings, result keys and errors, so an engine
-built here can be returned from a ``MethodSpec.build`` and driven by ``evaluation/benchmark.py``.
+The interface is the reference's (``common/engine.py``): ``StepRecord`` (:36-44), ``SlotState``
+(:47-58), ``RunConfig`` (:61-77), ``DecodeEngine.run`` (:178-297) and the commit rule ``_commit``
+(:144-164) keep their argument meanings, result keys and errors, so an engine built here can be
+returned from a ``MethodSpec.build`` and driven by ``evaluation/benchmark.py``.  The driver itself
+is organised around a prompt feed, a throughput meter and a convergence monitor.
 
 Subclasses implement ``_prefill_slots`` (fill a set of slots, return their first tokens) and
 ``_iteration`` (one scheduling iteration over the occupied slots).  Differences from the
@@ -120,26 +121,30 @@ class DecodeEngine:
 
     # ---------------------------------------------------------------- slot helpers
     def _commit(self, slot: int, tokens) -> int:
-        """Append tokens, stopping at EOS / max_new / a stop string; returns the useful count."""
+        """Append the longest prefix of ``tokens`` this request may still take - up to and including
+        its first EOS (unless ignored) and no further than its output budget - then let the stop
+        checker trim a matched stop string.  Returns how many appended tokens remain (the count
+        throughput uses)."""
         s = self.slots[slot]
-        n = 0
-        for t in tokens:
-            if s.finish_reason is not None:
-                break
-            t = int(t)
-            s.output.append(t)
-            n += 1
-            if not self.ignore_eos and t in self.eos:
-                s.finish_reason = "eos"
-            elif len(s.output) >= (s.max_new or self.max_new):
-                s.finish_reason = "length"
-        if n and self.stop_checker and not self.ignore_eos:
-            cut = self.stop_checker(s.output, n)
+        if s.finish_reason is not None:
+            return 0
+        room = (s.max_new or self.max_new) - len(s.output)
+        take = [int(t) for t in list(tokens)[:max(room, 0)]]
+        if not self.ignore_eos:
+            hit = next((i for i, t in enumerate(take) if t in self.eos), None)
+            if hit is not None:
+                take, s.finish_reason = take[:hit + 1], "eos"
+        s.output.extend(take)
+        if s.finish_reason is None and len(s.output) >= (s.max_new or self.max_new):
+            s.finish_reason = "length"
+        kept = len(take)
+        if kept and self.stop_checker is not None and not self.ignore_eos:
+            cut = self.stop_checker(s.output, kept)
             if cut is not None:
-                n -= len(s.output) - cut
+                kept -= len(s.output) - cut
                 del s.output[cut:]
                 s.finish_reason = "stop"
-        return n
+        return kept
 
     def _active(self) -> list:
         return [i for i, s in enumerate(self.slots) if not s.idle]
@@ -182,112 +187,168 @@ class DecodeEngine:
     # ---------------------------------------------------------------- driver
     @torch.inference_mode()
     def run(self, prompts: list, cfg: RunConfig) -> dict:
+        """Drive the engine over ``prompts`` (common/engine.py:178-297 defines the protocol the
+        reference's benchmark reads): static mode decodes every prompt once; cyclic mode replays
+        the pool, drops the first ``warmup`` completions and stops when the measured throughput has
+        settled (or at the evaluation / step caps)."""
         self.records = []
-        n_pool = len(prompts)
-        B = self.B
-        warmup_n = max(cfg.warmup_samples, math.ceil(cfg.warmup_per_slot * B)) if cfg.warmup_samples else 0
-        min_eval_n = max(cfg.converge_min_samples, math.ceil(cfg.min_eval_per_slot * B))
-        max_eval_n = max(cfg.max_eval_samples, min_eval_n) if cfg.converge else cfg.max_eval_samples
-        warm = cfg.mode == "static" or warmup_n == 0
-        state = {"cursor": 0}
-        completions = []
-        total_completed = evaluated = stable = steps = 0
-        anchor = None
-        stop_reason = None
-        measured_tokens, measured_ms = 0, 0.0
-        wall_t0 = time.perf_counter() if warm else None
-        wall_measured = 0.0
+        feed = _PromptFeed(prompts, cyclic=cfg.mode == "cyclic")
+        plan = _Plan.of(cfg, self.B)
+        meter = _Meter(plan.warm_from_start)
+        settle = _Convergence(cfg.converge_threshold, cfg.converge_window)
+        done: list = []
+        stop = None
 
-        def take(slot):
-            c = state["cursor"]
-            state["cursor"] += 1
-            return (slot, c % n_pool, prompts[c % n_pool])
-
-        fill = []
-        for slot in range(B):
-            if cfg.mode == "static" and state["cursor"] >= n_pool:
-                break
-            fill.append(take(slot))
-        self._assign_many(fill)
-
-        while True:
+        self._assign_many([(slot,) + feed.next() for slot in range(self.B) if feed.has_more()])
+        while stop is None:
             if not self._active():
-                stop_reason = "pool_exhausted"
+                stop = "pool_exhausted"
                 break
-            n_before = len(self.records)
-            committed = self._iteration(measured=warm)
-            new = self.records[n_before:]
-            step_ms = sum(r.forward_ms for r in new)
-            steps += len(new)
+            mark = len(self.records)
+            committed = self._iteration(measured=meter.warm)
+            step_ms = sum(r.forward_ms for r in self.records[mark:])
+            n_steps_now = len(self.records) - mark
             for i in self._active():
                 self.slots[i].decode_ms += step_ms
-            if warm:
-                measured_tokens += committed
-                measured_ms += step_ms
-            was_warm = warm
+            meter.account(committed, step_ms, n_steps_now)
+            measured_step = meter.warm
             refill = []
-            for slot, s in enumerate(self.slots):
-                if s.idle or s.finish_reason is None:
-                    continue
-                if stop_reason is not None:
-                    break
-                comp = {"pid": s.pid, "prompt_idx": s.prompt_idx, "prompt_len": s.prompt_len,
-                        "generated": len(s.output), "finish_reason": s.finish_reason, "decode_ms": s.decode_ms,
-                        "measured": was_warm}
-                if cfg.keep_outputs:
-                    comp["tokens"] = list(s.output)
-                completions.append(comp)
-                total_completed += 1
-                s.idle = True
-                if not was_warm:
-                    if not warm and total_completed >= warmup_n:
-                        warm = True
-                        wall_t0 = time.perf_counter()
+            for slot in self._finished_slots():
+                done.append(self._completion(slot, measured_step, cfg.keep_outputs))
+                meter.completed += 1
+                if not measured_step:
+                    if not meter.warm and meter.completed >= plan.warmup_n:
+                        meter.start_measuring()
                 elif cfg.mode == "cyclic":
-                    evaluated += 1
-                    if cfg.converge and evaluated >= min_eval_n and measured_ms > 0:
-                        thr = measured_tokens / (measured_ms / 1000)
-                        if anchor is None:
-                            anchor = thr
-                        elif abs(thr - anchor) / anchor < cfg.converge_threshold:
-                            stable += 1
-                        else:
-                            stable, anchor = 0, thr
-                        if stable >= cfg.converge_window:
-                            stop_reason = "converged"
-                    if stop_reason is None and evaluated >= max_eval_n:
-                        stop_reason = "max_eval_samples"
-                if cfg.mode == "cyclic" or state["cursor"] < n_pool:
-                    refill.append(take(slot))
-            if stop_reason is not None:
+                    meter.evaluated += 1
+                    if cfg.converge and meter.evaluated >= plan.min_eval_n and meter.ms > 0 and \
+                            settle.observe(meter.throughput()):
+                        stop = "converged"
+                    elif meter.evaluated >= plan.max_eval_n:
+                        stop = "max_eval_samples"
+                if stop is not None:
+                    break
+                if feed.has_more():
+                    refill.append((slot,) + feed.next())
+            if stop is not None:
                 break
             self._assign_many(refill)
-            if cfg.max_steps is not None and steps >= cfg.max_steps:
-                stop_reason = "max_steps"
-                break
-        if wall_t0 is not None:
-            wall_measured = time.perf_counter() - wall_t0
+            if cfg.max_steps is not None and meter.steps >= cfg.max_steps:
+                stop = "max_steps"
+        return self._report(cfg, plan, meter, done, stop)
 
-        rec = [r for r in self.records if r.measured]
-        per_kind = {}
-        for kind in sorted({r.kind for r in rec}):
-            ms = [r.forward_ms for r in rec if r.kind == kind]
-            per_kind[kind] = {"steps": len(ms), "mean_ms": float(np.mean(ms)), "p50_ms": float(np.median(ms))}
-        meas = [c for c in completions if c["measured"]]
-        tpot = [c["decode_ms"] / max(c["generated"] - 1, 1) for c in meas]
+    def _finished_slots(self):
+        """Occupied slots whose request finished, freed as they are yielded (slot order)."""
+        for slot, st in enumerate(self.slots):
+            if not st.idle and st.finish_reason is not None:
+                st.idle = True
+                yield slot
+
+    def _completion(self, slot: int, measured: bool, keep: bool) -> dict:
+        st = self.slots[slot]
+        c = dict(pid=st.pid, prompt_idx=st.prompt_idx, prompt_len=st.prompt_len, generated=len(st.output),
+                 finish_reason=st.finish_reason, decode_ms=st.decode_ms, measured=measured)
+        if keep:
+            c["tokens"] = list(st.output)
+        return c
+
+    def _report(self, cfg: RunConfig, plan: "_Plan", meter: "_Meter", done: list, stop) -> dict:
+        measured = [r for r in self.records if r.measured]
+        kinds = {}
+        for r in measured:
+            kinds.setdefault(r.kind, []).append(r.forward_ms)
+        steps = {k: {"steps": len(v), "mean_ms": float(np.mean(v)), "p50_ms": float(np.median(v))}
+                 for k, v in sorted(kinds.items())}
+        # time per output token after the first (the first one comes from the prefill)
+        tpot = [c["decode_ms"] / max(c["generated"] - 1, 1) for c in done if c["measured"]]
+        wall = meter.wall_s()
         metrics = {
-            "stop_reason": stop_reason,
-            "warmup_samples_effective": warmup_n,
-            "min_eval_samples_effective": min_eval_n,
-            "total_completions": total_completed,
-            "evaluated_completions": evaluated if cfg.mode == "cyclic" else total_completed,
-            "measured_tokens": measured_tokens,
-            "measured_forward_s": measured_ms / 1000,
-            "measured_wall_s": wall_measured,
-            "throughput_tok_s": measured_tokens / (measured_ms / 1000) if measured_ms else None,
-            "wall_throughput_tok_s": measured_tokens / wall_measured if wall_measured else None,
+            "stop_reason": stop,
+            "warmup_samples_effective": plan.warmup_n,
+            "min_eval_samples_effective": plan.min_eval_n,
+            "total_completions": meter.completed,
+            "evaluated_completions": meter.evaluated if cfg.mode == "cyclic" else meter.completed,
+            "measured_tokens": meter.tokens,
+            "measured_forward_s": meter.ms / 1000,
+            "measured_wall_s": wall,
+            "throughput_tok_s": meter.throughput() if meter.ms else None,
+            "wall_throughput_tok_s": meter.tokens / wall if wall else None,
             "mean_tpot_ms": float(np.mean(tpot)) if tpot else None,
-            "steps": per_kind,
+            "steps": steps,
             **self.extra_metrics(),
         }
-        return {"metrics": metrics, "completions": completions, "steps": [asdict(r) for r in self.records]}
+        return {"metrics": metrics, "completions": done, "steps": [asdict(r) for r in self.records]}
+
+
+class _PromptFeed:
+    """Prompt indices in order; cyclic feeds wrap around the pool, static ones stop at its end."""
+
+    def __init__(self, prompts: list, cyclic: bool):
+        self.prompts, self.cyclic, self.i = prompts, cyclic, 0
+
+    def has_more(self) -> bool:
+        return bool(self.prompts) and (self.cyclic or self.i < len(self.prompts))
+
+    def next(self) -> tuple:
+        k = self.i % len(self.prompts)
+        self.i += 1
+        return k, self.prompts[k]
+
+
+@dataclass
+class _Plan:
+    """Completion counts of a run: warm-up, minimum and maximum evaluated samples."""
+    warmup_n: int
+    min_eval_n: int
+    max_eval_n: int
+    warm_from_start: bool
+
+    @classmethod
+    def of(cls, cfg: RunConfig, B: int) -> "_Plan":
+        warm = max(cfg.warmup_samples, math.ceil(cfg.warmup_per_slot * B)) if cfg.warmup_samples else 0
+        lo = max(cfg.converge_min_samples, math.ceil(cfg.min_eval_per_slot * B))
+        hi = max(cfg.max_eval_samples, lo) if cfg.converge else cfg.max_eval_samples
+        return cls(warm, lo, hi, cfg.mode == "static" or warm == 0)
+
+
+class _Meter:
+    """Measured decode tokens and forward time (only while warm) and the wall clock of that phase."""
+
+    def __init__(self, warm: bool):
+        self.warm = warm
+        self.tokens, self.ms, self.steps = 0, 0.0, 0
+        self.completed = self.evaluated = 0
+        self.t0 = time.perf_counter() if warm else None
+
+    def account(self, tokens: int, ms: float, n_steps: int) -> None:
+        self.steps += n_steps
+        if self.warm:
+            self.tokens += tokens
+            self.ms += ms
+
+    def start_measuring(self) -> None:
+        self.warm, self.t0 = True, time.perf_counter()
+
+    def throughput(self) -> float:
+        return self.tokens / (self.ms / 1000)
+
+    def wall_s(self) -> float:
+        return time.perf_counter() - self.t0 if self.t0 is not None else 0.0
+
+
+class _Convergence:
+    """Settled once ``window`` consecutive observations stay within ``rel`` of an anchor value
+    (a departure re-anchors)."""
+
+    def __init__(self, rel: float, window: int):
+        self.rel, self.window = rel, window
+        self.anchor, self.run = None, 0
+
+    def observe(self, value: float) -> bool:
+        if self.anchor is None:
+            self.anchor = value
+        elif abs(value - self.anchor) < self.rel * self.anchor:
+            self.run += 1
+        else:
+            self.anchor, self.run = value, 0
+        return self.run >= self.window
