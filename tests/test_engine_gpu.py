@@ -100,13 +100,15 @@ def test_full_size_spec_equals_ar(cuda_dev, name, E, gamma, B, lens):
     assert res["metrics"]["spec"]["acceptance_rate"] > 0.2
 
 
+@pytest.mark.parametrize("schedule", ["lockstep", "unified"])
 @pytest.mark.parametrize("exits,grange,B,seed", [((1, 3, 5), (2, 8), 3, 0), ((2, 4), (0, 3), 4, 1), ((3,), (1, 1), 2, 2)])
-def test_dynamic_exit_and_draft_length_is_lossless(c1s_bf16, ar_reference, exits, grange, B, seed):
-    """Per-request exit layer and per-request, per-round draft length (coalesced ragged verify):
-    the output equals the AR output bit for bit whatever the draws."""
+def test_dynamic_exit_and_draft_length_is_lossless(c1s_bf16, ar_reference, exits, grange, B, seed, schedule):
+    """Per-request exit layer and per-request, per-round draft length (coalesced ragged verify), in
+    lock-step rounds or in the unified step (requests verify out of phase): the output equals the AR
+    output bit for bit whatever the draws."""
     prompts, ref = ar_reference
     eng = B200DynamicSpecEngine(c1s_bf16, B, 60, MAX_NEW, (2,), ignore_eos=True, exit_layers=exits,
-                                gamma_range=grange, policy_seed=seed)
+                                gamma_range=grange, policy_seed=seed, schedule=schedule)
     res = eng.run(prompts, RunConfig(mode="static", keep_outputs=True))
     eng.dm.check()
     assert _outputs(res) == ref

@@ -20,6 +20,7 @@ import pytest
 import torch
 
 from goldens import FULL_CASES, TOL, Golden, sparse_rel_err
+from thesis_b200.dynamic import B200DynamicSpecEngine
 from thesis_b200.eesd import B200ARBatchEngine, B200SpecEngine
 from thesis_b200.engine import RunConfig
 from thesis_b200.model import DeviceModel, ModelWeights
@@ -94,3 +95,21 @@ def test_engine_tokens_match_reference(cuda_dev, case):
         assert np.array_equal(ar, g["ar_tokens"])
         assert np.array_equal(sp, g["spec_tokens"])
         assert np.array_equal(sp, g["eesd_tokens"])
+
+
+@pytest.mark.parametrize("schedule", ["lockstep", "unified"])
+def test_dynamic_engine_matches_reference_ar_tokens_fp32(cuda_dev, case, schedule):
+    """Per-request exit layers {E/2, E, 3E/2 ...} and draft lengths 1..6 in fp32 at BASELINE
+    configuration 1: the tokens equal the reference's ARBatchEngine tokens."""
+    g, w = case
+    if g.dtype != "fp32":
+        pytest.skip("token identity with the reference is the fp32 contract")
+    L, E = w.cfg.n_layers, g.meta["exit_layer"]
+    exits = sorted({max(1, E // 2), E, min(L - 1, E + E // 2)})
+    prompts = [Prompt(f"p{i}", p) for i, p in enumerate(g.prompts())]
+    mp, B, n = max(len(p.tokens) for p in prompts), len(prompts), g.meta["max_new"]
+    eng = B200DynamicSpecEngine(w, B, mp, n, (), ignore_eos=True, exit_layers=exits, gamma_range=(1, 6),
+                                schedule=schedule)
+    got = _tokens(eng.run(prompts, RunConfig(mode="static", keep_outputs=True)), prompts)
+    eng.dm.check()
+    assert np.array_equal(got, g["ar_tokens"])

@@ -21,6 +21,13 @@ two changes, both expressed as packed ragged calls of the same kernels:
 Exit layers are drawn per request (deterministic in the prompt index and ``policy_seed``), draft
 lengths per request and round (a seeded generator).  Every kernel is batch-invariant, so the
 output is bit-identical to the autoregressive engine's whatever the draws.
+
+``schedule="unified"`` runs the reference's unified EESD step instead (solutions/engine.py:269-413
+with the fixed rule V = requests whose drafts reached their own length): every step is one shallow
+pass over all decoding requests - the drafting ones draft their next token, the ready ones run
+their last draft - followed, when some request is ready, by one deep pass over the ready requests
+only.  Requests verify out of phase, so a round no longer waits for the largest draw; instead most
+steps carry a deep pass over a few requests.
 """
 
 from __future__ import annotations
@@ -39,7 +46,10 @@ class B200DynamicSpecEngine(_B200Engine):
     name = "b200_layerskip_dynamic"
 
     def __init__(self, model, batch_size, max_prompt_len, max_new_tokens, eos_ids, *, exit_layers=(4, 8, 12),
-                 gamma_range=(2, 8), policy_seed: int = 0, **kw):
+                 gamma_range=(2, 8), policy_seed: int = 0, schedule: str = "lockstep", **kw):
+        if schedule not in ("lockstep", "unified"):
+            raise ValueError(f"schedule {schedule!r}: lockstep or unified")
+        self.schedule = schedule
         w = as_weights(model)
         exits = sorted({int(e) for e in exit_layers})
         if not exits or exits[0] < 1 or exits[-1] >= w.cfg.n_layers:
@@ -62,24 +72,31 @@ class B200DynamicSpecEngine(_B200Engine):
         self.stats = {"rounds": 0, "request_rounds": 0, "drafted": 0, "accepted": 0, "rejected": 0,
                       "draft_steps": 0, "draft_rows": 0, "deep_tokens": 0}
         self.exit_hist = {e: 0 for e in exits}
+        self.d = np.zeros(self.B, dtype=np.int64)       # unified: drafts of the current round so far
+        self.k_target = np.zeros(self.B, dtype=np.int64)  # unified: this round's draft length
 
     # ---------------------------------------------------------------- policy
     def _on_assigned(self, slot: int) -> None:
         idx = self.slots[slot].prompt_idx
         g = np.random.default_rng([self.policy_seed, int(idx)])
         self.exit_of[slot] = self.exits[int(g.integers(len(self.exits)))]
+        if self.schedule == "unified":
+            self.d[slot] = 0
+            self.k_target[slot] = int(self.draw_gammas(1)[0])
 
     def draw_gammas(self, n: int) -> np.ndarray:
         return self.rng.integers(self.g_lo, self.g_hi + 1, size=n)
 
     # ---------------------------------------------------------------- passes
-    def _shallow(self, sel: list, jj: list, pos: dict, draft: bool):
-        """Token jj[i] of request sel[i] through [0, exit): exit_h[s, j] = h, and with ``draft``
-        the head's argmax into seq_buf[s, j + 1].  Returns the KV positions read."""
+    def _shallow(self, sel: list, jj: list, pos: dict, draft):
+        """Token jj[i] of request sel[i] through [0, exit): exit_h[s, j] = h, and for the requests
+        that draft (``draft``: True = all, or a set of slots) the head's argmax into
+        seq_buf[s, j + 1].  Returns the KV positions read."""
         dm, cols = self.dm, self.cols
         order = sorted(range(len(sel)), key=lambda i: -int(self.exit_of[sel[i]]))
         sel = [sel[i] for i in order]
         jj = [int(jj[i]) for i in order]
+        drafting = sel if draft is True else [s for s in sel if draft and s in draft]
         n = len(sel)
         ex = np.array([self.exit_of[s] for s in sel], dtype=np.int64)
         blocks = [(s, pos[s] + j, 1) for s, j in zip(sel, jj)]
@@ -106,9 +123,17 @@ class B200DynamicSpecEngine(_B200Engine):
         self.h2d_bytes += 4 * 2 * n
         lib.call("eesd_copy_rows", self.dt_code, x.data_ptr(), None, self.exit_h.data_ptr(), src_d.data_ptr(), n,
                  self.cfg.dim, sp)
-        if draft:
+        if len(drafting) == n:
             d = dm.head_argmax(x)
             lib.call("eesd_scatter_ids", d.data_ptr(), dst_d.data_ptr(), self.seq_buf.data_ptr(), n, sp)
+        elif drafting:
+            # the drafting requests' rows of x and their seq_buf cells, in one small upload
+            who = set(drafting)
+            rows = np.array([i for i, s in enumerate(sel) if s in who], dtype=np.int32)
+            _, (rows_d, dsti_d) = dm.upload(dm.pack([(0, 0, 1)]), (rows, (src + 1)[rows]))
+            self.h2d_bytes += 4 * (2 * len(rows) + 7)
+            d = dm.head_argmax(x, rows_d)
+            lib.call("eesd_scatter_ids", d.data_ptr(), dsti_d.data_ptr(), self.seq_buf.data_ptr(), len(rows), sp)
         return kv
 
     def _deep(self, act: list, K: dict, pos: dict):
@@ -152,6 +177,62 @@ class B200DynamicSpecEngine(_B200Engine):
     # ---------------------------------------------------------------- one round
     @torch.inference_mode()
     def _iteration(self, measured: bool) -> int:
+        return self._unified_step(measured) if self.schedule == "unified" else self._lockstep_round(measured)
+
+    def _unified_step(self, measured: bool) -> int:
+        """One step of the unified schedule: the shallow pass of every decoding request, then the
+        deep pass of the requests whose drafts reached this round's length (solutions/engine.py:269-413
+        with V = {d >= k})."""
+        act = self._active()
+        pos = {s: int(self.slots[s].pos) for s in act}
+        ready = [s for s in act if self.d[s] >= self.k_target[s]]
+        drafting = {s for s in act if self.d[s] < self.k_target[s]}
+        iv = Interval(self.device).start()
+        kv = self._shallow(act, [int(self.d[s]) for s in act], pos, draft=drafting)
+        if not ready:
+            iv.stop()
+            self.records.append(StepRecord("draft", iv.ms, len(act), len(act), 0, kv, measured))
+            for s in drafting:
+                self.d[s] += 1
+            if measured:
+                self.stats["draft_steps"] += 1
+                self.stats["draft_rows"] += len(drafting)
+            return 0
+        K = {s: int(self.d[s]) for s in ready}
+        n, N, order, offs, kv_deep = self._deep(ready, K, pos)
+        iv.stop()
+        host = self.out_host[:n + N]
+        host.copy_(self.out[:n + N], non_blocking=True)
+        torch.cuda.current_stream().synchronize()           # the deep step's one device->host read
+        self.d2h_bytes += 4 * (n + N)
+        self.records.append(StepRecord("verify", iv.ms, len(act), len(act), N, kv + kv_deep, measured))
+        for s in drafting:
+            self.d[s] += 1
+        out = host.numpy()
+        acc_h, y_h = out[:n], out[n:n + N]
+        committed = 0
+        self.stats["rounds"] += 1
+        if measured and drafting:
+            self.stats["draft_rows"] += len(drafting)
+        for v, s in enumerate(order):
+            a = int(acc_h[v])
+            st = self.slots[s]
+            st.pos = pos[s] + a + 1
+            st.last_token = int(y_h[offs[v] + a])
+            committed += self._commit(s, y_h[offs[v]:offs[v] + a + 1].tolist())
+            if measured and st.finish_reason is None:
+                S = self.stats
+                S["request_rounds"] += 1
+                S["drafted"] += K[s]
+                S["accepted"] += a
+                S["rejected"] += K[s] - a
+                S["deep_tokens"] += K[s] + 1
+                self.exit_hist[int(self.exit_of[s])] += 1
+            self.d[s] = 0
+            self.k_target[s] = int(self.draw_gammas(1)[0])
+        return committed
+
+    def _lockstep_round(self, measured: bool) -> int:
         act = self._active()
         pos = {s: int(self.slots[s].pos) for s in act}
         ks = self.draw_gammas(len(act))
@@ -200,7 +281,7 @@ class B200DynamicSpecEngine(_B200Engine):
     def extra_metrics(self) -> dict:
         st = dict(self.stats)
         rr = max(st["request_rounds"], 1)
-        st.update(exit_layers=self.exits, gamma_range=[self.g_lo, self.g_hi],
+        st.update(exit_layers=self.exits, gamma_range=[self.g_lo, self.g_hi], schedule=self.schedule,
                   acceptance_rate=st["accepted"] / max(st["drafted"], 1),
                   tokens_per_verify=(st["accepted"] + st["request_rounds"]) / rr,
                   exit_hist={str(k): v for k, v in self.exit_hist.items()})

@@ -93,6 +93,9 @@ def _b200_dyn_args(g) -> None:
     g.add_argument("--b200-gamma-range", type=str, default="2,8",
                    help="[b200_layerskip_dynamic] draft length range lo,hi drawn per request and round")
     g.add_argument("--b200-policy-seed", type=int, default=0, help="[b200_layerskip_dynamic] draw seed")
+    g.add_argument("--b200-schedule", choices=("lockstep", "unified"), default="lockstep",
+                   help="[b200_layerskip_dynamic] lockstep rounds, or the unified step (each request verifies "
+                        "when its own draft length is reached)")
     _b200_ar_args(g)
 
 
@@ -108,6 +111,7 @@ def _b200_dyn_build(model, args, batch_size, max_prompt_len, eos):
         raise SystemExit("--b200-gamma-range takes lo,hi")
     return B200DynamicSpecEngine(model, batch_size, max_prompt_len, args.max_new_tokens, eos,
                                  exit_layers=_ints(args.b200_exit_layers), gamma_range=(g[0], g[1]),
+                                 schedule=getattr(args, "b200_schedule", "lockstep"),
                                  policy_seed=args.b200_policy_seed, **_kw(args))
 
 

@@ -54,8 +54,11 @@ def run_c4(args) -> dict:
     mp = max(len(p.tokens) for p in prompts)
     rc = RunConfig(mode="static", keep_outputs=True)
     out = {}
-    for name, make in (("dynamic", lambda: B200DynamicSpecEngine(w, args.requests, mp, args.new, (), ignore_eos=True,
-                                                                 exit_layers=(4, 8, 12), gamma_range=(2, 8))),
+    def dyn(schedule):
+        return lambda: B200DynamicSpecEngine(w, args.requests, mp, args.new, (), ignore_eos=True,
+                                             exit_layers=(4, 8, 12), gamma_range=(2, 8), schedule=schedule)
+
+    for name, make in (("dynamic", dyn("lockstep")), ("dynamic_unified", dyn("unified")),
                        ("ar", lambda: B200ARBatchEngine(w, args.requests, mp, args.new, (), ignore_eos=True))):
         eng = make()
         torch.cuda.synchronize()
@@ -70,11 +73,16 @@ def run_c4(args) -> dict:
         eng.free()
         del eng
         torch.cuda.empty_cache()
-    same = out["dynamic"].pop("tokens") == out["ar"].pop("tokens")
+    ar_tokens = out["ar"].pop("tokens")
+    same = out["dynamic"].pop("tokens") == ar_tokens
+    same_unified = out["dynamic_unified"].pop("tokens") == ar_tokens
     return {"workload": "c4", "metric": "generated tokens/s (decode device time), 1 GPU", "unit": "tokens/s",
-            "value": out["dynamic"]["throughput_tok_s"], "ar_value": out["ar"]["throughput_tok_s"],
+            "value": out["dynamic"]["throughput_tok_s"], "unified_value": out["dynamic_unified"]["throughput_tok_s"],
+            "ar_value": out["ar"]["throughput_tok_s"],
             "speedup_vs_ar": out["dynamic"]["throughput_tok_s"] / out["ar"]["throughput_tok_s"],
-            "identical_to_ar": same, "requests": args.requests, "new_tokens": args.new, "detail": out}
+            "unified_speedup_vs_ar": out["dynamic_unified"]["throughput_tok_s"] / out["ar"]["throughput_tok_s"],
+            "identical_to_ar": same, "unified_identical_to_ar": same_unified, "requests": args.requests,
+            "new_tokens": args.new, "detail": out}
 
 
 def run_c5(args) -> dict:
