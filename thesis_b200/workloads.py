@@ -1,9 +1,16 @@
 """Measurement of the BASELINE configurations beyond the headline one (one JSON line each).
 
+    python -m thesis_b200.workloads c2 [--requests 64] [--new 256]
     python -m thesis_b200.workloads c4 [--requests 32] [--new 256]
     python -m thesis_b200.workloads c5 [--requests 256] [--rate 40] [--budget 256]
     python -m thesis_b200.workloads strong [--rounds 20]
 
+c2  Llama3.2-1B shape (16 layers, dim 2048, 32 / 8 heads of 64, SwiGLU 8192, vocab 128256, tied
+    embeddings, RoPE theta 500000), bf16, residual outputs of layers >= 6 scaled by 0.1; batch 64,
+    prompt lengths uniform in 64..1024 (several 512-token prefill chunks), exit layer 6, gamma 6,
+    256 new tokens greedy, through the public engine API (``B200SpecEngine.run``), next to the
+    autoregressive engine on the same requests.  Reports decode throughput, the step p50s and the
+    verify step's fraction of its weight + KV HBM floor.
 c4  Llama2-7B shape (32 layers, dim 4096, 32 heads MHA of 128, SwiGLU 11008, vocab 32000, RoPE
     theta 10000), bf16, residual outputs of layers >= 4 scaled by 0.1; batch 32, prompt lengths
     lognormal (median 256, clipped to 32..1536), a per-request exit layer from {4, 8, 12} and a
@@ -85,6 +92,53 @@ def run_c4(args) -> dict:
             "new_tokens": args.new, "detail": out}
 
 
+def run_c2(args) -> dict:
+    from .eesd import B200ARBatchEngine, B200SpecEngine
+
+    cfg = preset("llama3-1b")
+    E, gamma = 6, 6
+    w = ModelWeights.synthetic(cfg, seed=0, dtype=torch.bfloat16, device="cuda", residual_scale_from=E,
+                               residual_scale=0.1)
+    prompts = synthetic_prompts(args.requests, cfg.vocab_size, seed=11, min_len=64, max_len=1024)
+    mp = max(len(p.tokens) for p in prompts)
+    rc = RunConfig(mode="static", keep_outputs=True)
+    out = {}
+    for name, make in (("spec", lambda: B200SpecEngine(w, args.requests, mp, args.new, (), ignore_eos=True,
+                                                       exit_layer=E, gamma=gamma)),
+                       ("ar", lambda: B200ARBatchEngine(w, args.requests, mp, args.new, (), ignore_eos=True))):
+        eng = make()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        res = eng.run(prompts, rc)
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+        m = res["metrics"]
+        toks = {c["pid"]: c["tokens"] for c in res["completions"]}
+        out[name] = {"throughput_tok_s": m["throughput_tok_s"], "e2e_tok_s": sum(len(t) for t in toks.values()) / wall,
+                     "steps": m["steps"], "spec": m.get("spec"), "tokens": toks}
+        eng.free()
+        del eng
+        torch.cuda.empty_cache()
+    same = out["spec"].pop("tokens") == out["ar"].pop("tokens")
+    # verify step floor: every layer's weights (the last draft through [0, E), the deep tokens through
+    # [E, L)), the LM head, and the batch's KV at the mean context in all layers, at the measured HBM peak
+    peaks_file = __import__("pathlib").Path(__file__).resolve().parents[1] / "MEASURED_PEAKS.json"
+    hbm = json.loads(peaks_file.read_text())["hbm_gbs"] if peaks_file.exists() else 6650.0
+    lens = np.array([len(p.tokens) for p in prompts])
+    ctx = float(lens.mean() + args.new / 2)
+    w_bytes = cfg.n_layers * cfg.layer_param_count * 2 + cfg.vocab_size * cfg.dim * 2
+    kv_bytes = cfg.n_layers * args.requests * ctx * cfg.kv_bytes_per_position_layer(2)
+    floor_ms = 1000 * (w_bytes + kv_bytes) / (hbm * 1e9)
+    v50 = out["spec"]["steps"]["verify"]["p50_ms"]
+    return {"workload": "c2", "metric": "generated tokens/s (decode device time), 1 GPU", "unit": "tokens/s",
+            "value": out["spec"]["throughput_tok_s"], "ar_value": out["ar"]["throughput_tok_s"],
+            "speedup_vs_ar": out["spec"]["throughput_tok_s"] / out["ar"]["throughput_tok_s"],
+            "identical_to_ar": same, "requests": args.requests, "new_tokens": args.new,
+            "verify_step": {"p50_ms": v50, "bytes": w_bytes + kv_bytes, "floor_ms": floor_ms, "frac": floor_ms / v50,
+                            "mean_context": ctx, "peak_gbs": hbm},
+            "detail": out}
+
+
 def run_c5(args) -> dict:
     from .serving import B200ServingEngine
 
@@ -146,7 +200,7 @@ def run_strong(args) -> dict:
 
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("workload", choices=["c4", "c5", "strong"])
+    ap.add_argument("workload", choices=["c2", "c4", "c5", "strong"])
     ap.add_argument("--rounds", type=int, default=20)
     ap.add_argument("--requests", type=int, default=None)
     ap.add_argument("--new", type=int, default=256)
@@ -156,8 +210,8 @@ def main(argv=None) -> None:
     ap.add_argument("--budget", type=int, default=256)
     args = ap.parse_args(argv)
     if args.requests is None:
-        args.requests = 32 if args.workload == "c4" else 256
-    res = {"c4": run_c4, "c5": run_c5, "strong": run_strong}[args.workload](args)
+        args.requests = {"c2": 64, "c4": 32}.get(args.workload, 256)
+    res = {"c2": run_c2, "c4": run_c4, "c5": run_c5, "strong": run_strong}[args.workload](args)
     print(json.dumps(res), flush=True)
 
 
