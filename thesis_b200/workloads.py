@@ -3,6 +3,7 @@
     python -m thesis_b200.workloads c2 [--requests 64] [--new 256]
     python -m thesis_b200.workloads c4 [--requests 32] [--new 256]
     python -m thesis_b200.workloads c5 [--requests 256] [--rate 40] [--budget 256]
+    torchrun --nproc-per-node 8 -m thesis_b200.workloads c5        # config 5 as specified: 8 GPUs
     python -m thesis_b200.workloads strong [--rounds 20]
 
 c2  Llama3.2-1B shape (16 layers, dim 2048, 32 / 8 heads of 64, SwiGLU 8192, vocab 128256, tied
@@ -21,7 +22,9 @@ c5  Llama3-8B shape, bf16, residual outputs of layers >= 8 scaled by 0.1; 256 sl
     arrivals at ``--rate`` requests/s, prompt lengths lognormal (median 512, clipped to 64..2048),
     output lengths uniform in 128..1024, exit layer 8, gamma 4, new-request prefill piggybacked
     on the draft/verify steps (``B200ServingEngine.run_poisson``).  Reports throughput, TTFT and
-    TPOT of the measured requests.
+    TPOT of the measured requests.  Under torchrun every rank serves its own request stream (the
+    requests shard across the GPUs, seeds differ per rank); rank 0 reports the aggregate wall-clock
+    throughput and every rank's latencies.
 
 strong  Strong scaling of config 3 (Llama3-8B shape, E=8, gamma=4, 64 requests in total, prompts
     U[128,512]) over 1, 2, 4 and 8 GPUs, measured shard by shard on one GPU: ranks share nothing
@@ -146,13 +149,15 @@ def run_c5(args) -> dict:
     w = ModelWeights.synthetic(cfg, seed=0, dtype=torch.bfloat16, device="cuda", residual_scale_from=8,
                                residual_scale=0.1)
     n_pool = args.requests + args.warm
-    base = synthetic_prompts(n_pool, cfg.vocab_size, seed=9, min_len=64, max_len=2048, lengths="lognormal",
-                             median=512)
-    rng = np.random.default_rng(9)
+    rank = int(__import__("os").environ.get("RANK", "0"))
+    base = synthetic_prompts(n_pool, cfg.vocab_size, seed=9 + 1000 * rank, min_len=64, max_len=2048,
+                             lengths="lognormal", median=512, pid_prefix=f"r{rank}p")
+    rng = np.random.default_rng(9 + 1000 * rank)
     prompts = [Prompt(p.pid, p.tokens, max_new=int(rng.integers(128, 1025))) for p in base]
     eng = B200ServingEngine(w, args.slots, 2048, 1024, (), ignore_eos=True, exit_layer=8, gamma=4,
                             piggyback_budget=args.budget)
-    res = eng.run_poisson(prompts, rate_per_s=args.rate, n_requests=args.requests, warm_requests=args.warm, seed=0)
+    res = eng.run_poisson(prompts, rate_per_s=args.rate, n_requests=args.requests, warm_requests=args.warm,
+                          seed=rank)
     eng.dm.check()
     m = res["metrics"]
     return {"workload": "c5", "metric": "generated tokens/s (wall clock, open loop), 1 GPU", "unit": "tokens/s",
@@ -198,6 +203,40 @@ def run_strong(args) -> dict:
             "unit": "tokens/s", "rounds": args.rounds, "rows": rows}
 
 
+def _multi_rank_c5(args) -> None:
+    """Config 5 over the ranks of a torchrun launch: one request stream per GPU, no collective on the
+    data path; the per-rank results are gathered once at the end."""
+    import datetime
+    import os
+
+    import torch.distributed as dist
+
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
+    try:
+        res = run_c5(args)
+        m = res["metrics"]
+        mine = {"rank": rank, "wall_tok_s": m["wall_throughput_tok_s"], "measured_tokens": m["measured_tokens"],
+                "wall_s": m["wall_s"], "decode_tok_s": m["throughput_tok_s"], "ttft_ms_mean": m["ttft_ms_mean"],
+                "ttft_ms_p99": m["ttft_ms_p99"], "tpot_ms_mean": m["tpot_ms_mean"], "tpot_ms_p99": m["tpot_ms_p99"],
+                "acceptance_rate": m["acceptance_rate"], "queue_left": m["queue_left"],
+                "requests_measured": m["evaluated_completions"]}
+        allr = [None] * world
+        dist.all_gather_object(allr, mine)
+        if rank == 0:
+            wall = max(r["wall_s"] for r in allr)
+            tokens = sum(r["measured_tokens"] for r in allr)
+            print(json.dumps({"workload": "c5", "metric": "generated tokens/s (wall clock, open loop), all GPUs",
+                              "unit": "tokens/s", "value": tokens / wall, "n_gpus": world, "slots_per_gpu": args.slots,
+                              "rate_per_s_per_gpu": args.rate, "requests_per_gpu": args.requests, "ranks": allr}),
+                  flush=True)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("workload", choices=["c2", "c4", "c5", "strong"])
@@ -211,6 +250,9 @@ def main(argv=None) -> None:
     args = ap.parse_args(argv)
     if args.requests is None:
         args.requests = {"c2": 64, "c4": 32}.get(args.workload, 256)
+    if args.workload == "c5" and int(__import__("os").environ.get("WORLD_SIZE", "1")) > 1:
+        _multi_rank_c5(args)
+        return
     res = {"c2": run_c2, "c4": run_c4, "c5": run_c5, "strong": run_strong}[args.workload](args)
     print(json.dumps(res), flush=True)
 
