@@ -331,7 +331,13 @@ __global__ void __launch_bounds__(WARPS * 32, MINB) attn_bf16_kernel(const __gri
   uint64_t* full = reinterpret_cast<uint64_t*>(Qs + RMAX * LDQ);   // [NS]
   volatile int* abort_flag = reinterpret_cast<volatile int*>(full + NS);
 
-  const int item = blockIdx.x, kvh = blockIdx.y;
+  // grid (KV heads, items): the CTAs of one item are consecutive and items run in `order`
+  const int kvh = blockIdx.x;
+  const int item = g.order ? g.order[blockIdx.y] : (int)blockIdx.y;
+  if (item < 0 || item >= g.n_items) {
+    if (threadIdx.x == 0) set_status(status, kStatusBadIndex);
+    return;
+  }
   const int b = items[2 * item], t0 = items[2 * item + 1];
   if (b < 0 || b >= g.n_blocks) {
     if (threadIdx.x == 0) set_status(status, kStatusBadIndex);
@@ -928,9 +934,11 @@ int launch_attention(int dtype, const AttnGeom& g_in, const void* q, const void*
   AttnGeom g = g_in;
   g.status = status;
   g.spin = spin_limit();
+  g.n_items = n_items;
   dim3 grid(n_items, g.n_kv_heads);
   if (dtype == EESD_BF16) {
-    if (!kmap || !vmap) return EESD_ERR_ARG;
+    if (!kmap || !vmap || n_items > 65535) return EESD_ERR_ARG;
+    grid = dim3(g.n_kv_heads, n_items);
     // rows per item <= 16: 4 warps, 2 stages, 3 CTAs per SM; else 8 warps, 3 stages, 2 per SM
     const bool small = rows_max <= 16;
     int rc;
@@ -963,6 +971,42 @@ int launch_attention(int dtype, const AttnGeom& g_in, const void* q, const void*
       return EESD_ERR_ARG;
     }
   }
+  return launched();
+}
+
+// One CTA: item i's slot is the number of items that run before it (more keys, or as many keys
+// and a lower index), so the slots form a permutation whatever the lengths are.  An item whose
+// block index is out of range sorts last; the attention kernel reports it.
+__global__ void __launch_bounds__(1024) attn_order_kernel(const int32_t* __restrict__ blk,
+                                                          const int32_t* __restrict__ items, int n_items, int n_blocks,
+                                                          int item_tokens, int32_t* __restrict__ order) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ int keys[kAttnOrderMax];
+  for (int i = threadIdx.x; i < n_items; i += blockDim.x) {
+    const int b = items[2 * i], t0 = items[2 * i + 1];
+    int len = -1;
+    if (b >= 0 && b < n_blocks) len = blk[4 * b + 3] + t0 + min(item_tokens, blk[4 * b + 1] - t0);
+    keys[i] = len;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < n_items; i += blockDim.x) {
+    const int li = keys[i];
+    int slot = 0;
+    for (int k = 0; k < n_items; ++k) {
+      const int lk = keys[k];
+      slot += (lk > li) | ((lk == li) & (k < i));
+    }
+    order[slot] = i;
+  }
+}
+
+int launch_attn_order(const int32_t* blk, const int32_t* items, int n_items, int n_blocks, int n_heads, int n_kv_heads,
+                      int32_t* order, cudaStream_t s) {
+  if (n_items <= 0) return EESD_OK;
+  if (n_items > kAttnOrderMax) return EESD_ERR_ARG;
+  launch_pdl(attn_order_kernel, dim3(1), dim3(1024), 0, s, blk, items, n_items, n_blocks,
+             attn_item_tokens(n_heads, n_kv_heads), order);
   return launched();
 }
 

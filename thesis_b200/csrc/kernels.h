@@ -15,6 +15,8 @@ struct AttnGeom {
   int n_tokens, n_blocks;   // of the packed batch: items and blocks are checked against them
   uint32_t spin;     // poll limit of the key-tile waits (spin_limit())
   int* status;       // device status word (fp32 kernel; the bf16 kernel takes it as an argument)
+  int n_items = 0;                  // work items of the launch (set by launch_attention)
+  const int32_t* order = nullptr;   // bf16 kernel: item of each grid slot (launch_attn_order), or identity
 };
 
 int attn_item_tokens(int n_heads, int n_kv_heads);
@@ -45,6 +47,11 @@ int launch_attention(int dtype, const AttnGeom& g, const void* q, const void* kc
                      const int32_t* blk, const int32_t* items, int n_items, int max_ctx, int* status, cudaStream_t s,
                      const CUtensorMap* kmap, const CUtensorMap* vmap, int layer, const AttnAppend& app = AttnAppend(),
                      int rows_max = 32);   // rows_max: largest item's query rows (tokens x GQA group)
+// order[j] = the item the bf16 attention grid runs j-th: items by descending key count (ties by
+// index), so the longest start in the first wave.  At most kAttnOrderMax items.
+constexpr int kAttnOrderMax = 4096;
+int launch_attn_order(const int32_t* blk, const int32_t* items, int n_items, int n_blocks, int n_heads, int n_kv_heads,
+                      int32_t* order, cudaStream_t s);
 int launch_embed(int dtype, const void* table, const int32_t* ids, int n, int dim, int vocab, void* x, int* status,
                  cudaStream_t s);
 int launch_copy_rows(int dtype, const void* src, const int32_t* src_idx, void* dst, const int32_t* dst_idx, int n,

@@ -65,6 +65,7 @@ struct Model {
   // workspace pieces
   int* status;
   void *xn, *qkv, *attn, *act;
+  int32_t* attn_order;          // bf16 attention: item of each grid slot, longest first
   float* gu;                    // fp32 path: [max_tokens, 2 I]
   float* logits32;              // fp32 path: [kHeadChunk, vocab]
   unsigned long long* keys;
@@ -79,7 +80,7 @@ struct Model {
 constexpr int kHeadChunk = 128;
 
 struct Layout {
-  size_t status, xn, qkv, attn, act, gu, logits32, keys, partials, partial_bytes, total;
+  size_t status, xn, qkv, attn, act, gu, logits32, keys, order, partials, partial_bytes, total;
 };
 
 Layout layout_for(const EesdModelDesc& d) {
@@ -96,6 +97,7 @@ Layout layout_for(const EesdModelDesc& d) {
   L.gu = c.take(d.dtype == EESD_F32 ? T * 2 * d.intermediate * 4 : 0);
   L.logits32 = c.take(d.dtype == EESD_F32 ? (size_t)kHeadChunk * d.vocab * 4 : 0);
   L.keys = c.take(T * 8);
+  L.order = c.take((size_t)kAttnOrderMax * 4);
   if (d.dtype == EESD_BF16) {
     // split-K scratch that covers every projection at up to max_tokens tokens (the LM head is
     // never split)
@@ -225,6 +227,7 @@ int eesd_model_create(const EesdModelDesc* d, void** out) {
   m->gu = reinterpret_cast<float*>(ws + L.gu);
   m->logits32 = reinterpret_cast<float*>(ws + L.logits32);
   m->keys = reinterpret_cast<unsigned long long*>(ws + L.keys);
+  m->attn_order = reinterpret_cast<int32_t*>(ws + L.order);
   m->gemm_scratch.partials = ws + L.partials;
   m->gemm_scratch.partial_bytes = L.partial_bytes;
   if (d->dtype == EESD_BF16) {
@@ -295,6 +298,13 @@ int eesd_forward_layers(void* h, void* x, const EesdBatch* b, int start, int end
   // query rows of the largest attention work item: one token per block (draft) or up to a full item
   const int G = d.n_heads / d.n_kv_heads;
   const int rows_max = b->n_tokens == b->n_blocks ? G : attn_item_tokens(d.n_heads, d.n_kv_heads) * G;
+  if (d.dtype == EESD_BF16 && b->n_items <= kAttnOrderMax) {
+    // every layer's attention grid runs the batch's work items longest first
+    rc = launch_attn_order(b->blk, b->items, b->n_items, b->n_blocks, d.n_heads, d.n_kv_heads, m->attn_order, s);
+    m->launches++;
+    if (rc) return fail(rc, "attention order launch");
+    g.order = m->attn_order;
+  }
   for (int i = start; i < end; ++i) {
     uint8_t* kc = static_cast<uint8_t*>(d.k_cache) + (size_t)i * layer_kv;
     uint8_t* vc = static_cast<uint8_t*>(d.v_cache) + (size_t)i * layer_kv;
