@@ -93,6 +93,13 @@ class ClockSampler:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
                                           "--format=csv,noheader,nounits", "-lms", "50"], stdout=self.fh,
                                          stderr=subprocess.DEVNULL)
+            # nvidia-smi takes a moment to start: wait (at most 5 s) for its first sample, so that a
+            # short timed region still falls inside the sampled window
+            t_end = time.time() + 5.0
+            while time.time() < t_end and self.proc.poll() is None:
+                if Path(self.path).stat().st_size > 0:
+                    break
+                time.sleep(0.02)
         except Exception:
             self.proc = None
         return self
@@ -379,11 +386,12 @@ def run_ours(args) -> None:
         gather_outputs({ids[i]: eng.slots[i].output for i in range(nb)}, n_total, world, device=dev)
     stream = torch.cuda.current_stream()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
     committed = 0
     with ClockSampler(local) as clk:
+        # the sampler is running before the ranks line up, so its start-up is outside the timed region
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
         torch.cuda.nvtx.range_push("timed")          # lets a profiler select exactly the timed rounds
         ev0.record(stream)
         for _ in range(args.steps):
