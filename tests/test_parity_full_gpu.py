@@ -6,7 +6,8 @@ the unmodified reference, ``tests/golden/make_golden.py``).
   prompts of 32..128 tokens, exit layer 4, draft length 4, 64 new tokens.  Prefill, exit-layer and
   final logits within 1e-4; AR and speculative token sequences identical to the reference's
   ``ARBatchEngine``, ``SyncSpecEngine`` and ``EESDEngine`` (common/engine.py:302-436,
-  solutions/engine.py:269-489).
+  solutions/engine.py:269-489), and so are the dynamic-exit engine's (both schedules) and the
+  serving engine's with piggybacked prefill.
 * ``c3s_bf16``: the Llama3-8B shape (dim 4096, GQA 4, head_dim 128, SwiGLU 14336, vocab 128256,
   untied head) cut to 4 layers, bf16, prompts of 137..1027 tokens (multi-chunk prefill, contexts over
   16 key tiles, split-K projections, CTA-pair W13, two-tile LM head).  Logits within 2e-2; the
@@ -24,6 +25,7 @@ from thesis_b200.dynamic import B200DynamicSpecEngine
 from thesis_b200.eesd import B200ARBatchEngine, B200SpecEngine
 from thesis_b200.engine import RunConfig
 from thesis_b200.model import DeviceModel, ModelWeights
+from thesis_b200.serving import B200ServingEngine
 from thesis_b200.synthetic import Prompt
 
 pytestmark = pytest.mark.gpu
@@ -112,4 +114,23 @@ def test_dynamic_engine_matches_reference_ar_tokens_fp32(cuda_dev, case, schedul
                                 schedule=schedule)
     got = _tokens(eng.run(prompts, RunConfig(mode="static", keep_outputs=True)), prompts)
     eng.dm.check()
+    assert np.array_equal(got, g["ar_tokens"])
+
+
+@pytest.mark.parametrize("budget", [24, 1000])
+def test_piggyback_engine_matches_reference_ar_tokens_fp32(cuda_dev, case, budget):
+    """Two slots for four requests, so the later prompts are prefilled in chunks of at most
+    `budget` tokens riding on the other requests' draft and verify steps (config 5's serving
+    engine), fp32 at BASELINE configuration 1: the tokens equal the reference's ARBatchEngine
+    tokens."""
+    g, w = case
+    if g.dtype != "fp32":
+        pytest.skip("token identity with the reference is the fp32 contract")
+    prompts = [Prompt(f"p{i}", p) for i, p in enumerate(g.prompts())]
+    mp, n = max(len(p.tokens) for p in prompts), g.meta["max_new"]
+    eng = B200ServingEngine(w, 2, mp, n, (), ignore_eos=True, exit_layer=g.meta["exit_layer"], gamma=g.meta["gamma"],
+                            piggyback_budget=budget)
+    got = _tokens(eng.run(prompts, RunConfig(mode="static", keep_outputs=True)), prompts)
+    eng.dm.check()
+    assert eng.stats["piggyback_tokens"] > 0
     assert np.array_equal(got, g["ar_tokens"])
