@@ -5,6 +5,7 @@
     python -m thesis_b200.workloads c5 [--requests 256] [--rate 40] [--budget 256]
     torchrun --nproc-per-node 8 -m thesis_b200.workloads c5        # config 5 as specified: 8 GPUs
     python -m thesis_b200.workloads strong [--rounds 20]
+    python -m thesis_b200.workloads lossless [--new 512]
 
 c2  Llama3.2-1B shape (16 layers, dim 2048, 32 / 8 heads of 64, SwiGLU 8192, vocab 128256, tied
     embeddings, RoPE theta 500000), bf16, residual outputs of layers >= 6 scaled by 0.1; batch 64,
@@ -32,6 +33,10 @@ strong  Strong scaling of config 3 (Llama3-8B shape, E=8, gamma=4, 64 requests i
     (`bench.py --strong --gpus N` runs them concurrently).  For each N every shard runs 3 warm-up
     and ``--rounds`` timed draft/verify rounds (CUDA events); the aggregate is all shards' tokens
     over the slowest shard's time, as in the bench.
+
+lossless  Config 3 in full (Llama3-8B shape, bf16, 64 requests, prompts U[128,512], E=8, gamma=4,
+    ``--new`` tokens): the speculative engine's output against the autoregressive engine's, token
+    for token, for every request (the bench line checks a subset only).
 
 Weights and prompts are seeded synthetic stand-ins for the checkpoints and datasets the
 reference would use; no dataset item is reproduced.
@@ -203,6 +208,43 @@ def run_strong(args) -> dict:
             "unit": "tokens/s", "rounds": args.rounds, "rows": rows}
 
 
+def run_lossless(args) -> dict:
+    from .eesd import B200ARBatchEngine, B200SpecEngine
+
+    cfg = preset("llama3-8b")
+    w = ModelWeights.synthetic(cfg, seed=0, dtype=torch.bfloat16, device="cuda", residual_scale_from=8,
+                               residual_scale=0.1)
+    prompts = synthetic_prompts(64, cfg.vocab_size, seed=1000, min_len=128, max_len=512)
+    rc = RunConfig(mode="static", keep_outputs=True)
+    out = {}
+    for name, make in (("ar", lambda: B200ARBatchEngine(w, 64, 512, args.new, (), ignore_eos=True)),
+                       ("spec", lambda: B200SpecEngine(w, 64, 512, args.new, (), ignore_eos=True, exit_layer=8,
+                                                       gamma=4))):
+        eng = make()
+        res = eng.run(prompts, rc)
+        eng.dm.check()
+        out[name] = {c["pid"]: list(c["tokens"]) for c in res["completions"]}
+        out[name + "_metrics"] = res["metrics"]
+        eng.free()
+        del eng
+        torch.cuda.empty_cache()
+    same = [out["ar"][p.pid] == out["spec"][p.pid] for p in prompts]
+    first_diff = None
+    for p in prompts:
+        a, b = out["ar"][p.pid], out["spec"][p.pid]
+        if a != b:
+            first_diff = {"pid": p.pid, "index": next(i for i in range(min(len(a), len(b)) + 1)
+                                                      if i >= min(len(a), len(b)) or a[i] != b[i])}
+            break
+    sm = out["spec_metrics"]
+    return {"workload": "lossless", "config": "C3: Llama3-8B shape, bf16, 64 requests, prompts U[128,512], E=8, "
+                                              f"gamma=4, {args.new} new tokens",
+            "requests": len(prompts), "tokens_per_request": args.new,
+            "identical_requests": int(sum(same)), "spec_equals_ar": all(same), "first_difference": first_diff,
+            "acceptance_rate": sm.get("spec", {}).get("acceptance_rate"),
+            "spec_throughput_tok_s": sm.get("throughput_tok_s"), "ar_throughput_tok_s": out["ar_metrics"].get("throughput_tok_s")}
+
+
 def _multi_rank_c5(args) -> None:
     """Config 5 over the ranks of a torchrun launch: one request stream per GPU, no collective on the
     data path; the per-rank results are gathered once at the end."""
@@ -239,10 +281,10 @@ def _multi_rank_c5(args) -> None:
 
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("workload", choices=["c2", "c4", "c5", "strong"])
+    ap.add_argument("workload", choices=["c2", "c4", "c5", "strong", "lossless"])
     ap.add_argument("--rounds", type=int, default=20)
     ap.add_argument("--requests", type=int, default=None)
-    ap.add_argument("--new", type=int, default=256)
+    ap.add_argument("--new", type=int, default=None, help="new tokens per request (lossless: 512, else 256)")
     ap.add_argument("--rate", type=float, default=40.0)
     ap.add_argument("--slots", type=int, default=256)
     ap.add_argument("--warm", type=int, default=16)
@@ -250,10 +292,12 @@ def main(argv=None) -> None:
     args = ap.parse_args(argv)
     if args.requests is None:
         args.requests = {"c2": 64, "c4": 32}.get(args.workload, 256)
+    if args.new is None:
+        args.new = 512 if args.workload == "lossless" else 256
     if args.workload == "c5" and int(__import__("os").environ.get("WORLD_SIZE", "1")) > 1:
         _multi_rank_c5(args)
         return
-    res = {"c2": run_c2, "c4": run_c4, "c5": run_c5, "strong": run_strong}[args.workload](args)
+    res = {"c2": run_c2, "c4": run_c4, "c5": run_c5, "strong": run_strong, "lossless": run_lossless}[args.workload](args)
     print(json.dumps(res), flush=True)
 
 
