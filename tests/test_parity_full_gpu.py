@@ -14,6 +14,8 @@ the unmodified reference, ``tests/golden/make_golden.py``).
   speculative output equals this engine's own AR output (lossless).
 * ``c2s_bf16``: the same for the Llama3.2-1B shape (dim 2048, GQA 4, head_dim 64, SwiGLU 8192,
   tied head), 4 layers, bf16, draft length 6, prompts of 64..1024 tokens.
+* ``c4s_bf16``: the same for the Llama2-7B shape (MHA: 32 KV heads of 128, SwiGLU 11008,
+  vocabulary 32000, RoPE theta 10000), 4 layers, bf16, prompts of 40..1020 tokens.
 
 Relative error = max |a - b| / max |b| over the stored logits columns.
 """
