@@ -6,6 +6,7 @@
     torchrun --nproc-per-node 8 -m thesis_b200.workloads c5        # config 5 as specified: 8 GPUs
     python -m thesis_b200.workloads strong [--rounds 20]
     python -m thesis_b200.workloads lossless [--new 512]
+    python -m thesis_b200.workloads refgpu [--new 512]
 
 c2  Llama3.2-1B shape (16 layers, dim 2048, 32 / 8 heads of 64, SwiGLU 8192, vocab 128256, tied
     embeddings, RoPE theta 500000), bf16, residual outputs of layers >= 6 scaled by 0.1; batch 64,
@@ -37,6 +38,11 @@ strong  Strong scaling of config 3 (Llama3-8B shape, E=8, gamma=4, 64 requests i
 lossless  Config 3 in full (Llama3-8B shape, bf16, 64 requests, prompts U[128,512], E=8, gamma=4,
     ``--new`` tokens): the speculative engine's output against the autoregressive engine's, token
     for token, for every request (the bench line checks a subset only).
+
+refgpu  Config 3 through the reference's OWN packed engine (``solutions/engine.py`` EESDEngine,
+    fixed schedule, gamma 4, exit layer 8: PyTorch eager with cuBLAS and SDPA) on this GPU, on
+    the same synthetic weights (shared, not copied) and prompts, next to this library's engine.
+    The reference is imported from ``baseline/_ref`` (``baseline/install_reference.sh``).
 
 Weights and prompts are seeded synthetic stand-ins for the checkpoints and datasets the
 reference would use; no dataset item is reproduced.
@@ -245,6 +251,77 @@ def run_lossless(args) -> dict:
             "spec_throughput_tok_s": sm.get("throughput_tok_s"), "ar_throughput_tok_s": out["ar_metrics"].get("throughput_tok_s")}
 
 
+def run_refgpu(args) -> dict:
+    import statistics
+    import sys
+    from pathlib import Path
+
+    from .eesd import B200SpecEngine
+
+    ref = Path(__file__).resolve().parents[1] / "baseline" / "_ref"
+    if not (ref / "solutions" / "engine.py").exists():
+        return {"workload": "refgpu", "unavailable": "the reference is not installed under baseline/_ref"}
+    sys.path.insert(0, str(ref))
+    from common.data import Prompt as RefPrompt
+    from common.model import LayerSkipLlama, LayerWeights, ModelConfig as RefConfig
+    from solutions.cost_model import synthetic_cost_model
+    from solutions.engine import EESDEngine, EngineConfig
+
+    cfg = preset("llama3-8b")
+    w = ModelWeights.synthetic(cfg, seed=0, dtype=torch.bfloat16, device="cuda", residual_scale_from=8,
+                               residual_scale=0.1)
+    prompts = synthetic_prompts(64, cfg.vocab_size, seed=1000, min_len=128, max_len=512)
+    t = w.t
+    rc = RefConfig(vocab_size=cfg.vocab_size, dim=cfg.dim, n_layers=cfg.n_layers, n_heads=cfg.n_heads,
+                   n_kv_heads=cfg.n_kv_heads, head_dim=cfg.head_dim, intermediate_size=cfg.intermediate_size,
+                   norm_eps=cfg.norm_eps, rope_theta=cfg.rope_theta, max_position_embeddings=2048,
+                   tie_word_embeddings=cfg.tie_word_embeddings, rope_scaling=cfg.rope_scaling)
+    layers = [LayerWeights(wqkv=t[f"l{i}.wqkv"], wo=t[f"l{i}.wo"], w13=t[f"l{i}.w13"], w2=t[f"l{i}.w2"],
+                           attn_norm=t[f"l{i}.attn_norm"], ffn_norm=t[f"l{i}.ffn_norm"]) for i in range(cfg.n_layers)]
+    model = LayerSkipLlama(rc, t["embed"], layers, t["norm"], t["lm_head"], w.device, torch.bfloat16, 2048)
+    rp = [RefPrompt(p.pid, list(p.tokens)) for p in prompts]
+    eng = EESDEngine(model, 64, 512, args.new, (), EngineConfig(mode="spec", sched="fixed", gamma=4, k=8),
+                     synthetic_cost_model(model.cfg))
+    res = eng.run(rp, "static", keep_outputs=True)
+    m = res["metrics"]
+    deep = [r.ms for r in eng.records if r.kind == "deep" and r.measured]
+    shallow = [r.ms for r in eng.records if r.kind == "shallow" and r.measured]
+    ref_tok = {c["pid"]: list(c["tokens"]) for c in res["completions"]}
+    del eng, model
+    torch.cuda.empty_cache()
+    ours = B200SpecEngine(w, 64, 512, args.new, (), ignore_eos=True, exit_layer=8, gamma=4)
+    r2 = ours.run(prompts, RunConfig(mode="static", keep_outputs=True))
+    ours.dm.check()
+    om = r2["metrics"]
+    same = sum(ref_tok.get(c["pid"]) == list(c["tokens"]) for c in r2["completions"])
+
+    def common_prefix(a, b):
+        n = 0
+        while n < min(len(a), len(b)) and a[n] == b[n]:
+            n += 1
+        return n
+    prefix = [common_prefix(ref_tok.get(c["pid"], []), list(c["tokens"])) for c in r2["completions"]]
+    return {"workload": "refgpu", "config": f"C3: Llama3-8B shape, bf16, 64 requests, prompts U[128,512], E=8, "
+                                            f"gamma=4, {args.new} new tokens, static mode, one B200",
+            "reference": {"engine": "solutions/engine.py EESDEngine (fixed, gamma 4, k 8)",
+                          "throughput_tok_s": m["throughput_tok_s"], "wall_throughput_tok_s": m["wall_throughput_tok_s"],
+                          "verify_step_p50_ms": statistics.median(deep) if deep else None,
+                          "draft_step_p50_ms": statistics.median(shallow) if shallow else None,
+                          "acceptance_rate": m["acceptance_rate"]},
+            "ours": {"engine": "thesis_b200 B200SpecEngine", "throughput_tok_s": om["throughput_tok_s"],
+                     "wall_throughput_tok_s": om.get("wall_throughput_tok_s"),
+                     "verify_step_p50_ms": om["steps"]["verify"]["p50_ms"],
+                     "draft_step_p50_ms": om["steps"]["draft"]["p50_ms"],
+                     "acceptance_rate": om["spec"]["acceptance_rate"]},
+            "speedup_decode": om["throughput_tok_s"] / m["throughput_tok_s"] if m["throughput_tok_s"] else None,
+            "speedup_wall": (om["wall_throughput_tok_s"] / m["wall_throughput_tok_s"]
+                             if om.get("wall_throughput_tok_s") and m["wall_throughput_tok_s"] else None),
+            "requests_with_identical_tokens": int(same),
+            "common_prefix_tokens": {"mean": float(np.mean(prefix)), "min": int(min(prefix)), "max": int(max(prefix))},
+            "note": "both in bf16 with different kernels; bf16 outputs may differ after a near-tie, so identical "
+                    "tokens are counted, not required"}
+
+
 def _multi_rank_c5(args) -> None:
     """Config 5 over the ranks of a torchrun launch: one request stream per GPU, no collective on the
     data path; the per-rank results are gathered once at the end."""
@@ -281,7 +358,7 @@ def _multi_rank_c5(args) -> None:
 
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("workload", choices=["c2", "c4", "c5", "strong", "lossless"])
+    ap.add_argument("workload", choices=["c2", "c4", "c5", "strong", "lossless", "refgpu"])
     ap.add_argument("--rounds", type=int, default=20)
     ap.add_argument("--requests", type=int, default=None)
     ap.add_argument("--new", type=int, default=None, help="new tokens per request (lossless: 512, else 256)")
@@ -293,11 +370,12 @@ def main(argv=None) -> None:
     if args.requests is None:
         args.requests = {"c2": 64, "c4": 32}.get(args.workload, 256)
     if args.new is None:
-        args.new = 512 if args.workload == "lossless" else 256
+        args.new = 512 if args.workload in ("lossless", "refgpu") else 256
     if args.workload == "c5" and int(__import__("os").environ.get("WORLD_SIZE", "1")) > 1:
         _multi_rank_c5(args)
         return
-    res = {"c2": run_c2, "c4": run_c4, "c5": run_c5, "strong": run_strong, "lossless": run_lossless}[args.workload](args)
+    res = {"c2": run_c2, "c4": run_c4, "c5": run_c5, "strong": run_strong, "lossless": run_lossless,
+           "refgpu": run_refgpu}[args.workload](args)
     print(json.dumps(res), flush=True)
 
 
