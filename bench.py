@@ -335,6 +335,23 @@ def algorithmic(kind: str, n_tok: int, cfg, ctx: float, eb: int = 2) -> tuple[fl
     return float(2 * n_tok * dim * eb), 0.0
 
 
+def kernel_floor_ms(cfg, hbm: float, tflops: float, kv_layer: float, layers_by_tokens, head_tokens) -> float:
+    """Floor of a step (ms): the sum over its kernels of max(algorithmic bytes / HBM peak, FLOPs /
+    sustained bf16 peak).  layers_by_tokens: (layers, packed tokens) segments; kv_layer: one layer's
+    KV bytes for the batch; head_tokens: the token count of each LM-head call.  At 320 tokens the
+    projections and the head are tensor-bound, so this floor is above the bytes-only one."""
+    t = 0.0
+    for n_layers, n_tok in layers_by_tokens:
+        for kind in ("gemm_qkv", "gemm_o", "gemm_w13", "gemm_w2"):
+            by, fl = algorithmic(kind, n_tok, cfg, 0.0)
+            t += n_layers * max(by / hbm, fl / tflops)
+        t += n_layers * kv_layer / hbm
+    for n_tok in head_tokens:
+        by, fl = algorithmic("head", n_tok, cfg, 0.0)
+        t += max(by / hbm, fl / tflops)
+    return 1000 * t
+
+
 def run_ours(args) -> None:
     import numpy as np
     import torch
@@ -464,27 +481,13 @@ def run_ours(args) -> None:
 
     tflops = pk["bf16_tflops_sustained"] * 1e12
 
-    def kernel_floor_ms(layers_by_tokens, head_tokens):
-        """Sum over the step's kernels of max(algorithmic bytes / HBM peak, FLOPs / sustained bf16
-        peak): at 320 tokens the projections and the head are tensor-bound, so this floor is
-        above the bytes-only one."""
-        t = 0.0
-        for n_layers, n_tok in layers_by_tokens:
-            for kind in ("gemm_qkv", "gemm_o", "gemm_w13", "gemm_w2"):
-                by, fl = algorithmic(kind, n_tok, cfg, 0.0)
-                t += n_layers * max(by / hbm, fl / tflops)
-            t += n_layers * kv_layer / hbm
-        for n_tok in head_tokens:
-            by, fl = algorithmic("head", n_tok, cfg, 0.0)
-            t += max(by / hbm, fl / tflops)
-        return 1000 * t
-
     def step_roof(nbytes, ms, kfloor):
         return {"bytes": nbytes, "floor_ms": 1000 * nbytes / hbm, "measured_ms": ms,
                 "frac": (1000 * nbytes / hbm) / ms if ms else None,
                 "kernel_floor_ms": kfloor, "frac_of_kernel_floor": kfloor / ms if ms else None}
-    kf_draft = kernel_floor_ms([(EXIT, nb)], [nb])
-    kf_verify = kernel_floor_ms([(EXIT, nb), (L - EXIT, nb * (GAMMA + 1))], [nb * (GAMMA + 1)])
+    kf_draft = kernel_floor_ms(cfg, hbm, tflops, kv_layer, [(EXIT, nb)], [nb])
+    kf_verify = kernel_floor_ms(cfg, hbm, tflops, kv_layer, [(EXIT, nb), (L - EXIT, nb * (GAMMA + 1))],
+                                [nb * (GAMMA + 1)])
     share = {f"{k}@{n}": round(v[1] / total_ms, 4) for (k, n), v in sorted(groups.items(), key=lambda kv: -kv[1][1])}
 
     # ---- losslessness on the headline workload: the speculative output of a fixed subset of the

@@ -175,3 +175,27 @@ print("registered", sorted(m for m in METHODS if m.startswith("b200")))
     r = subprocess.run([sys.executable, "-c", code], cwd=str(ref), capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stderr[-3000:]
     assert "b200_layerskip_dynamic" in r.stdout
+
+
+def test_bench_kernel_floor():
+    """The bench's per-kernel floor: at 64 tokens every projection is HBM-bound, so the floor is the
+    bytes-only one; at 320 tokens the projections and the head are tensor-bound and it is higher."""
+    import sys
+    from pathlib import Path
+
+    sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+    import bench
+    from thesis_b200.config import preset
+
+    cfg = preset("llama3-8b")
+    hbm, tf = 6549.4e9, 1400.3e12
+    kv = bench.algorithmic("attn", 1, cfg, 576 * 64)[0]
+    gemms = ("gemm_qkv", "gemm_o", "gemm_w13", "gemm_w2")
+    bytes_64 = sum(bench.algorithmic(k, 64, cfg, 0.0)[0] for k in gemms) + kv
+    f64 = bench.kernel_floor_ms(cfg, hbm, tf, kv, [(1, 64)], [])
+    assert abs(f64 - 1000 * bytes_64 / hbm) < 1e-9
+    f320 = bench.kernel_floor_ms(cfg, hbm, tf, kv, [(1, 320)], [])
+    flops_320 = sum(bench.algorithmic(k, 320, cfg, 0.0)[1] for k in gemms)
+    assert abs(f320 - 1000 * (flops_320 / tf + kv / hbm)) < 1e-9 and f320 > f64
+    verify = bench.kernel_floor_ms(cfg, hbm, tf, kv, [(8, 64), (24, 320)], [320])
+    assert 3.5 < verify < 4.5          # ms, against a bytes-only floor of ~2.8 ms
