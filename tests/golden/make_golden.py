@@ -23,7 +23,8 @@ Full-size cases (``FULL_CASES``) run the benchmark shapes: BASELINE configuratio
 4-layer Llama3-8B-shaped bf16 model with prompts of 137..1027 tokens (several 64-key tiles, split-K
 projections, the CTA-pair W13, the two-tile LM head, multi-chunk prefill on the B200 side), and the
 same for the Llama3.2-1B shape (head_dim 64 attention, its split-K shapes, the tied head) and the
-Llama2-7B shape (MHA, SwiGLU 11008, vocabulary 32000).  Their
+Llama2-7B shape (MHA, SwiGLU 11008, vocabulary 32000), and the 4-layer Llama3-8B case in fp32
+(token identity at long contexts).  Their
 weights are regenerated from the seed by ``thesis_b200.synthetic``; their logits rows (vocabulary
 128256) are stored sparsely: every 16th column plus each row's 64 largest entries
 (``<key>_stride``, ``<key>_top_idx``, ``<key>_top_val``).
@@ -73,6 +74,10 @@ FULL_CASES = [
     # bf16, draft length 6; contexts up to ~1030 tokens
     dict(name="c2s_bf16", preset="llama3-1b", overrides=dict(n_layers=4), dtype="bf16", exit_layer=2, gamma=6,
          weights=dict(residual_scale_from=2, residual_scale=0.1), lens=(64, 333, 702, 1024), max_new=12,
+         max_seq=1088),
+    # Llama3-8B shape cut to 4 layers in fp32: token identity at long contexts and head_dim 128
+    dict(name="c3s_fp32", preset="llama3-8b", overrides=dict(n_layers=4), dtype="fp32", exit_layer=2, gamma=4,
+         weights=dict(residual_scale_from=2, residual_scale=0.1), lens=(137, 449, 700, 1027), max_new=12,
          max_seq=1088),
     # Llama2-7B shape (BASELINE configuration 4's model: MHA, SwiGLU 11008, vocab 32000, RoPE theta
     # 10000) cut to 4 layers, bf16; contexts up to ~1030 tokens

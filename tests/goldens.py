@@ -10,7 +10,7 @@ import numpy as np
 GOLDEN = Path(__file__).resolve().parent / "golden"
 CASES = ["tiny_fp32", "tiny_bf16", "c1s_fp32", "c1s_bf16", "d128_fp32", "mha_bf16"]
 # benchmark-shaped cases with sparsely stored logits (every 16th column + each row's top 64)
-FULL_CASES = ["c1_fp32", "c3s_bf16", "c2s_bf16", "c4s_bf16"]
+FULL_CASES = ["c1_fp32", "c3s_bf16", "c3s_fp32", "c2s_bf16", "c4s_bf16"]
 
 # Tolerances from the task statement: logits agree within 1e-4 relative in fp32 and 2e-2 in
 # bf16.  "Relative" is max |a - b| / max |b| over the compared tensor.

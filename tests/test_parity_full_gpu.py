@@ -12,6 +12,8 @@ the unmodified reference, ``tests/golden/make_golden.py``).
   untied head) cut to 4 layers, bf16, prompts of 137..1027 tokens (multi-chunk prefill, contexts over
   16 key tiles, split-K projections, CTA-pair W13, two-tile LM head).  Logits within 2e-2; the
   speculative output equals this engine's own AR output (lossless).
+* ``c3s_fp32``: the same model in fp32: logits within 1e-4, and AR, speculative, dynamic-exit and
+  piggyback tokens identical to the reference's at contexts up to ~1040 tokens and head_dim 128.
 * ``c2s_bf16``: the same for the Llama3.2-1B shape (dim 2048, GQA 4, head_dim 64, SwiGLU 8192,
   tied head), 4 layers, bf16, draft length 6, prompts of 64..1024 tokens.
 * ``c4s_bf16``: the same for the Llama2-7B shape (MHA: 32 KV heads of 128, SwiGLU 11008,
