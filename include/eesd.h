@@ -238,6 +238,10 @@ int eesd_gemm(int dtype, int epilogue, const void* x, const void* w, const void*
  * wait give up at once.  A wait that gives up sets a timeout bit in the device status word, the
  * kernel lets the copies and MMAs it already issued land, and returns. */
 #define EESD_OPT_SPIN_LIMIT 6
+/* EESD_OPT_MMA_SPLIT: a bf16 GEMM token tile above 256 tokens on one CTA takes two MMAs per K16
+ * step; this sets the first one's N (a multiple of 16, default 192), the second takes the rest.
+ * 0 = two equal halves.  Numerics-neutral. */
+#define EESD_OPT_MMA_SPLIT 7
 int eesd_set_option(int option, int value);
 
 /* Exit head that allocates nothing, for callers that cannot call cudaMalloc (a serving

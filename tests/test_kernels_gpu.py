@@ -77,6 +77,27 @@ def test_gemm_bf16_is_batch_invariant(cuda_dev, mma_n):
         lib.call("eesd_set_option", lib.OPT_MMA_N, 0)
 
 
+@pytest.mark.parametrize("n_tok", [257, 320, 352, 384])
+def test_gemm_two_mma_split_is_bit_identical(cuda_dev, n_tok):
+    """A token tile above 256 tokens takes two MMAs per k-step; their N split (192 + rest by
+    default, equal halves, 256 + rest) changes no bit of the result."""
+    g = torch.Generator(device=cuda_dev).manual_seed(n_tok)
+    k, n_out = 4096, 4096
+    x = torch.randn(n_tok, k, device=cuda_dev, generator=g).bfloat16()
+    w = (torch.randn(n_out, k, device=cuda_dev, generator=g) * 0.02).bfloat16()
+    r = torch.randn(n_tok, n_out, device=cuda_dev, generator=g).bfloat16()
+    outs = []
+    try:
+        for split in (192, 0, 256, 128):
+            lib.call("eesd_set_option", lib.OPT_MMA_SPLIT, split)
+            outs.append((_gemm(x, w), _gemm(x, w, lib.EPI_RESIDUAL, residual=r)))
+    finally:
+        lib.call("eesd_set_option", lib.OPT_MMA_SPLIT, 192)
+    for y, z in outs[1:]:
+        assert torch.equal(y, outs[0][0]) and torch.equal(z, outs[0][1])
+    _close(outs[0][0], x.float() @ w.float().T, 1e-2)
+
+
 def test_gemm_swiglu_on_cta_pairs(cuda_dev):
     """W13 + SwiGLU at the 8B shape runs on CTA pairs (cta_group::2, M = 256, each CTA loading half
     of the token tile): it matches the fp32 reference and the single-CTA kernel, and a token row's

@@ -58,6 +58,7 @@ struct alignas(8) TcParams {
   int a_packed;     // 1: weight in tile-packed layout (3-D map over 16 KB tiles), 0: row-major 2-D map
   int acc_cols;     // TMEM columns of the accumulator (bn, or 2 bn for SwiGLU)
   int res_stage;    // split-K RESIDUAL: the owned slice's residual rows arrive by bulk copies (256 B each)
+  int mma_n1;       // > 0: two MMAs per k-step, N = mma_n1 then bn - mma_n1 (token tiles above 256)
   const bf16* residual;
   int ld_res;
   bf16* y;
@@ -263,6 +264,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       // small token counts): loop-invariant values live in registers, descriptors are built once
       // per stage and stepped by adding to their 14-bit start-address field (bytes / 16).
       const uint32_t idesc = idesc_bf16_f32(PAIR ? 2 * kBM : kBM, p.mma_n);
+      const uint32_t idesc1 = idesc_bf16_f32(kBM, p.mma_n1 > 0 ? p.mma_n1 : 16);
+      const uint32_t idesc2 = idesc_bf16_f32(kBM, p.mma_n1 > 0 ? p.bn - p.mma_n1 : 16);
       const int stages = p.stages, bn = p.bn, mma_n = p.mma_n;
       const uint32_t full0 = smem_u32(full), empty0 = smem_u32(empty);
       const uint64_t desc_hi = sw128_kmajor_desc(0);
@@ -289,6 +292,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (PAIR) {   // one MMA per accumulator spans the whole token tile (mma_n == bn <= 256)
             tc_mma_f16_pair(tmem_base, a_k, b_k, idesc, acc);
             if (kNA == 2) tc_mma_f16_pair(tmem_base + bn, a_k + (kATileBytes >> 4), b_k, idesc, acc);
+          } else if (p.mma_n1 > 0) {
+            tc_mma_f16(tmem_base, a_k, b_k, idesc1, acc);
+            tc_mma_f16(tmem_base + p.mma_n1, a_k, b_k + (uint64_t)(p.mma_n1 * 8), idesc2, acc);
           } else {
             for (int nb = 0; nb < bn; nb += mma_n, b_k += sub_lo) {
               tc_mma_f16(tmem_base + nb, a_k, b_k, idesc, acc);
@@ -601,6 +607,10 @@ int g_splits_option = 0;  // 0: split count from the weight shape
 int g_stages_option = 0;  // 0: as many stages as the shared-memory budget holds
 int g_pair_option = 1;    // 1: SwiGLU GEMMs whose row tiles pair up run on CTA pairs (cta_group::2)
 int g_head_two_option = 1;  // 1: head launches of up to 256 tokens take two row tiles per CTA
+// Token tiles above 256 on one CTA take two MMAs per k-step.  Equal halves (e.g. 160 + 160 at 320
+// tokens) measured slower than 192 + 128 (or 256 + 64): 250.4 -> 235.5 us per 320-token layer,
+// bit-identical.  0 restores equal halves.
+int g_split_n_option = 192;
 
 int next_pow2(int v) {
   int p = 32;
@@ -739,6 +749,7 @@ void tc_set_splits(int n) { g_splits_option = n; }
 void tc_set_stages(int n) { g_stages_option = n; }
 void tc_set_pair(int n) { g_pair_option = n; }
 void tc_set_head_two_tiles(int n) { g_head_two_option = n; }
+void tc_set_split_n(int n) { g_split_n_option = n; }
 
 TcPlan tc_plan(int n_tok, int n_out, int k, int epi) {
   TcPlan pl{};
@@ -830,6 +841,14 @@ int tc_gemm_launch(int epi, const CUtensorMap& map_w, const void* x, int n_tok, 
   p.tmem_cols = pl.tmem_cols;
   p.a_packed = a_packed;
   p.acc_cols = pl.acc_cols;
+  {
+    const int n1 = g_split_n_option, n2 = pl.bn - n1;
+    const bool kna1 = !(epi == EESD_EPI_SWIGLU || pl.argmax2);
+    p.mma_n1 = (n1 > 0 && kna1 && !pl.pair && pl.bn > 256 && pl.mma_n * 2 == pl.bn && n1 % 16 == 0 && n2 % 16 == 0 &&
+                n1 <= 256 && n2 >= 16 && n2 <= 256)
+                   ? n1
+                   : 0;
+  }
   // residual rows of an owned slice by 256-byte bulk copies: whole 128-row tiles, 16-byte aligned rows
   p.res_stage = epi == EESD_EPI_RESIDUAL && n_out % kBM == 0 && ld_res % 8 == 0 &&
                 (reinterpret_cast<uintptr_t>(residual) & 15) == 0;

@@ -37,6 +37,7 @@ void tc_set_splits(int n);
 void tc_set_stages(int n);
 void tc_set_pair(int n);
 void tc_set_head_two_tiles(int n);
+void tc_set_split_n(int n);
 // a_packed = 1: map_w is a tile-packed weight map (encode_packed_map), else a row-major 2-D map
 int tc_gemm_launch(int epi, const CUtensorMap& map_w, const void* x, int n_tok, int n_out, int k, int up_offset,
                    const void* residual, int ld_res, void* y, int ld_y, unsigned long long* keys, int* status,

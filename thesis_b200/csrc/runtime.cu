@@ -677,6 +677,11 @@ int eesd_set_option(int option, int value) {
     tc_set_head_two_tiles(value);
     return EESD_OK;
   }
+  if (option == 7) {   // N of the first of two MMAs per k-step for token tiles above 256 (default 192; 0: halves)
+    if (value < 0 || value > 256 || value % 16) return fail(EESD_ERR_ARG, "split n %d", value);
+    tc_set_split_n(value);
+    return EESD_OK;
+  }
   if (option == 6) {   // pipeline-wait poll limit: -1 = the default, n >= 0 = n polls (0: every wait gives up)
     if (value < -1) return fail(EESD_ERR_ARG, "spin limit %d", value);
     g_spin_limit = value < 0 ? kSpinLimit : (uint32_t)value;

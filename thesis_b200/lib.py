@@ -13,7 +13,7 @@ LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libeesd.so"
 OK, ERR_ARG, ERR_CUDA, ERR_DEVICE = 0, 1, 2, 3
 BF16, F32 = 0, 1
 EPI_STORE, EPI_RESIDUAL, EPI_SWIGLU = 0, 1, 2
-OPT_MMA_N, OPT_SPLITS, OPT_STAGES, OPT_PAIR, OPT_HEAD_TWO_TILES, OPT_SPIN_LIMIT = 1, 2, 3, 4, 5, 6
+OPT_MMA_N, OPT_SPLITS, OPT_STAGES, OPT_PAIR, OPT_HEAD_TWO_TILES, OPT_SPIN_LIMIT, OPT_MMA_SPLIT = 1, 2, 3, 4, 5, 6, 7
 PROF_KINDS = 9
 PROF_NAMES = ["norm", "gemm_qkv", "rope_kv", "attn", "gemm_o", "gemm_w13", "gemm_w2", "head", "misc"]
 
