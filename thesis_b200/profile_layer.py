@@ -1,6 +1,6 @@
 """Small, self-contained profiling workload for single-kernel captures (ncu) of the hot path.
 
-    python -m thesis_b200.profile_layer [--iters N] [--layers 2] [--ctx 300 700] [--prefill]
+    python -m thesis_b200.profile_layer [--iters N] [--layers 2] [--ctx 300 700] [--prefill] [--mma-split N]
 
 Builds a LayerSkip-Llama3-8B-shaped model with only ``--layers`` layers (random bf16 weights,
 about 2 GB on the device with the KV cache), fills the KV cache with random values, and runs a
