@@ -9,7 +9,8 @@ the exit head on both, ``--iters`` times, then the same again under per-launch C
 prints the average time of every (kernel kind, token count).  Inputs are larger than L2 (436 MB
 of weights per layer, ~130 MB of KV per attention launch).  ``--prefill`` adds a prefill-shaped
 call (4 requests x 512 prompt tokens from position 0), which runs the separate RoPE/KV-append
-kernel.
+kernel.  ``--mma-split N`` sets the N of the first of the two MMAs a k-step issues for token tiles
+above 256 (``EESD_OPT_MMA_SPLIT``; 0 = two equal halves).
 """
 
 from __future__ import annotations
@@ -30,7 +31,12 @@ def main(argv=None) -> None:
     ap.add_argument("--layers", type=int, default=2)
     ap.add_argument("--ctx", type=int, nargs=2, default=(300, 700))
     ap.add_argument("--prefill", action="store_true")
+    ap.add_argument("--mma-split", type=int, default=None)
     args = ap.parse_args(argv)
+    if args.mma_split is not None:
+        from . import lib
+
+        lib.call("eesd_set_option", lib.OPT_MMA_SPLIT, args.mma_split)
     cfg = replace(preset("llama3-8b"), n_layers=args.layers)
     w = ModelWeights.synthetic(cfg, seed=0, dtype=torch.bfloat16, device="cuda")
     dm = DeviceModel(w, max_batch=64, max_seq=max(args.ctx[1], 512) + 64, max_tokens=2048 if args.prefill else 512)
